@@ -1,0 +1,355 @@
+// Weight-stationary GEMMs for the decode / prefill path:
+//     Y[t, n] = epilogue( sum_k X[t, k] * W[n, k] )
+// W is an nn.Linear weight [N_out, K] (row-major, K contiguous), X the activations
+// [T, K]. On the tensor-core path the weight tile is the UMMA "A" operand (M = 128
+// rows) and a tile of BN tokens is "B" (N = BN), so one CTA streams a 128-row weight
+// slice once and reuses it for BN tokens; both operands arrive by TMA with 128-byte
+// swizzle and the fp32 accumulator lives in TMEM. Several independent problems (e.g.
+// lin1/lin2/lin3 of one layer, which read different inputs) share one launch.
+//
+// Epilogues restate the reference's rounding points for the op that follows each
+// GEMM (one/modeling_one.py:343-391, 559-573; one/linear_moe.py:93).
+#pragma once
+
+#include "common.cuh"
+
+namespace one {
+
+enum EpiKind : int {
+  EPI_STORE = 0,    // out = rnd(acc + bias)                                  (nn.Linear)
+  EPI_HXPRE = 1,    // out = rnd(aux + clamp(rnd(acc + bias), +-100))         (hx + hx_moe, :559,563)
+  EPI_XMOE = 2,     // out = rnd(aux * clamp(rnd(acc + bias), +-100))         (mean * x_moe, :560,568)
+  EPI_CX = 3,       // out = rnd(acc + bias); out2 = clamp(out, +-1e4)        (cx_moe, then LinearMoE clamp)
+  EPI_GELU_UP = 4,  // rows interleaved (gate j, up j): out[j] = rnd(rnd(gelu(g)) * u)  (OneMLP, :205-206)
+  EPI_PARTIAL = 5,  // fp32 split-K partial: ws[split][t][n] = acc
+  EPI_ARGMAX = 6,   // logits v = rnd(acc): per-token (max v, lowest n) by 64-bit atomicMax
+};
+
+constexpr int kMaxProblems = 4;
+
+struct GemmProblem {
+  int kind;
+  int Nw;            // weight rows
+  int K;
+  int T;             // tokens
+  int m_tiles, n_tiles, splits, kb_per_split;
+  int tile_begin;    // first linear CTA index of this problem
+  const void* bias;  // [Nw] model dtype, or null
+  void* out;
+  int ldo;
+  void* out2;
+  int ldo2;
+  const void* aux;
+  int lda;
+  float* ws;         // EPI_PARTIAL: [splits][T][ldw]
+  int ldw;
+  unsigned long long* best;  // EPI_ARGMAX: [T]
+};
+
+struct __align__(64) GemmParams {
+  CUtensorMap tmw[kMaxProblems];  // weights, box {64, 128}
+  CUtensorMap tmx[kMaxProblems];  // activations, box {64, BN}
+  GemmProblem prob[kMaxProblems];
+  int nprob;
+  int total_tiles;
+  DevErr* err;
+};
+
+// Plain-pointer view for the SIMT path (fp32 models).
+struct SimtGemmParams {
+  const void* w[kMaxProblems];
+  const void* x[kMaxProblems];
+  int ldx[kMaxProblems];
+  GemmProblem prob[kMaxProblems];
+  int nprob;
+  int total_tiles;
+};
+
+// ------------------------------------------------------------------ epilogue (per element)
+// argmax key: order-preserving bits of the rounded logit above the inverted index, so a
+// larger key is a larger value and, among equal values, the lower vocabulary index
+// (torch.argmax returns the first maximum).
+template <typename T>
+ONE_DEVINL unsigned long long argmax_key(float v, int n);
+template <>
+ONE_DEVINL unsigned long long argmax_key<__nv_bfloat16>(float v, int n) {
+  uint32_t b = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+  b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+}
+template <>
+ONE_DEVINL unsigned long long argmax_key<float>(float v, int n) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+}
+
+template <typename T>
+ONE_DEVINL float bias_at(const GemmProblem& P, int n) {
+  return P.bias ? ld<T>(reinterpret_cast<const T*>(P.bias) + n) : 0.0f;
+}
+
+// All kinds except GELU_UP / ARGMAX, one (n, t) element. Caller guarantees n < Nw, t < T.
+template <typename T>
+ONE_DEVINL void epi_elem(const GemmProblem& P, int n, int t, float acc, int split) {
+  switch (P.kind) {
+    case EPI_STORE: {
+      st<T>(reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n, acc + bias_at<T>(P, n));
+      break;
+    }
+    case EPI_HXPRE: {
+      float y = fminf(fmaxf(rnd<T>(acc + bias_at<T>(P, n)), -100.f), 100.f);
+      float a = ld<T>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n);
+      st<T>(reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n, a + y);
+      break;
+    }
+    case EPI_XMOE: {
+      float y = fminf(fmaxf(rnd<T>(acc + bias_at<T>(P, n)), -100.f), 100.f);
+      float a = ld<T>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n);
+      st<T>(reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n, a * y);
+      break;
+    }
+    case EPI_CX: {
+      float y = rnd<T>(acc + bias_at<T>(P, n));
+      st<T>(reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n, y);
+      st<T>(reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n, fminf(fmaxf(y, -1e4f), 1e4f));
+      break;
+    }
+    case EPI_PARTIAL: {
+      P.ws[((size_t)split * P.T + t) * P.ldw + n] = acc;
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+// OneMLP on an interleaved gate/up weight: packed row 2j is gate_proj row j, 2j+1 is
+// up_proj row j. Bias (mlp_bias) is interleaved the same way.
+template <typename T>
+ONE_DEVINL void epi_gelu_pair(const GemmProblem& P, int n_even, int t, float g, float u) {
+  float gb = rnd<T>(g + bias_at<T>(P, n_even));
+  float ub = rnd<T>(u + bias_at<T>(P, n_even + 1));
+  float a = rnd<T>(gelu_erf(gb));
+  st<T>(reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + (n_even >> 1), a * ub);
+}
+
+// ------------------------------------------------------------------ tensor-core kernel
+template <int BN>
+struct TcCfg {
+  static constexpr int kStages = BN >= 256 ? 3 : 4;
+  static constexpr int kABytes = 128 * 64 * 2;
+  static constexpr int kBBytes = BN * 64 * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kThreads = 192;  // w0 TMA, w1 MMA + TMEM owner, w2..5 epilogue
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
+  using C = TcCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* accb = empty + C::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+
+  // linear tile -> (problem, split, m tile, n tile); n fastest so the CTAs that share a
+  // weight slice run together and the slice is fetched from HBM once.
+  const int tile = blockIdx.x;
+  int pi = 0;
+  while (pi + 1 < p.nprob && tile >= p.prob[pi + 1].tile_begin) ++pi;
+  const GemmProblem& P = p.prob[pi];
+  int local = tile - P.tile_begin;
+  const int n_tile = local % P.n_tiles;
+  local /= P.n_tiles;
+  const int m_tile = local % P.m_tiles;
+  const int split = local / P.m_tiles;
+  const int kb_total = (P.K + 63) / 64;
+  const int kb0 = split * P.kb_per_split;
+  const int nkb = min(kb0 + P.kb_per_split, kb_total) - kb0;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmw[pi]);
+    tma_prefetch_desc(&p.tmx[pi]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto sA = [&](int s) { return smem + s * C::kStageBytes; };
+  auto sB = [&](int s) { return smem + s * C::kStageBytes + C::kABytes; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Weights do not depend on the previous kernel: request the first stages before
+      // waiting on it, so the HBM stream overlaps the previous kernel's tail.
+      const uint64_t wpol = l2_policy_evict_first();
+      const int pre = min(nkb, C::kStages);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+        tma_load_2d_hint(sA(i), &p.tmw[pi], &full[i], (kb0 + i) * 64, m_tile * 128, wpol);
+      }
+      pdl_wait();
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % C::kStages;
+        const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
+        if (i >= pre) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          tma_load_2d_hint(sA(s), &p.tmw[pi], &full[s], (kb0 + i) * 64, m_tile * 128, wpol);
+        }
+        tma_load_2d(sB(s), &p.tmx[pi], &full[s], (kb0 + i) * 64, n_tile * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % C::kStages;
+        const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
+        if (!mbar_wait(&full[s], ph, p.err, 2)) break;
+        tc_fence_after();
+        const uint64_t ad = umma_desc_sw128(sA(s));
+        const uint64_t bd = umma_desc_sw128(sB(s));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 per 64-wide stage; +32 B per step
+          umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accb);
+    }
+  } else {
+    // epilogue warps 2..5; TMEM lane quarter is fixed by warp id % 4
+    pdl_wait();
+    const int q = warp & 3;
+    const int n = m_tile * 128 + q * 32 + lane;
+    const bool nvalid = n < P.Nw;
+    const bool ok = mbar_wait(accb, 0, p.err, 3);
+    tc_fence_after();
+    if (ok) {
+      pdl_launch_dependents();
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        const int t0 = n_tile * BN + c0;
+        if (t0 >= P.T) break;  // warp-uniform
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld_wait();
+        const int tn = min(16, P.T - t0);
+        if (P.kind == EPI_GELU_UP) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
+            if (nvalid && !(n & 1) && j < tn) epi_gelu_pair<__nv_bfloat16>(P, n, t0 + j, v[j], other);
+          }
+        } else if (P.kind == EPI_ARGMAX) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            unsigned long long key = nvalid ? argmax_key<__nv_bfloat16>(v[j], n) : 0ull;
+            if (nvalid && P.out && j < tn)
+              st<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(P.out) + (size_t)(t0 + j) * P.ldo + n, v[j]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, key, o);
+              key = ok2 > key ? ok2 : key;
+            }
+            if (lane == 0 && j < tn && key) atomicMax(P.best + t0 + j, key);
+          }
+        } else if (nvalid) {
+          for (int j = 0; j < tn; ++j) epi_elem<__nv_bfloat16>(P, n, t0 + j, v[j], split);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+// ------------------------------------------------------------------ SIMT kernel (fp32 models)
+// 64 weight rows x 64 tokens per CTA, 256 threads, 4x4 outputs per thread, K staged in
+// shared memory 16 at a time. Rows of a thread are 4 consecutive n, so an interleaved
+// gate/up pair always sits in one thread.
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtGemmParams p, DevErr* err) {
+  __shared__ float sW[16][65];
+  __shared__ float sX[16][65];
+  pdl_wait();
+  const int tile = blockIdx.x;
+  int pi = 0;
+  while (pi + 1 < p.nprob && tile >= p.prob[pi + 1].tile_begin) ++pi;
+  const GemmProblem& P = p.prob[pi];
+  int local = tile - P.tile_begin;
+  const int n_tile = local % P.n_tiles;
+  local /= P.n_tiles;
+  const int m_tile = local % P.m_tiles;
+  const int split = local / P.m_tiles;
+  const int k0 = split * P.kb_per_split * 64;
+  const int k1 = min(P.K, k0 + P.kb_per_split * 64);
+  const T* W = reinterpret_cast<const T*>(p.w[pi]);
+  const T* X = reinterpret_cast<const T*>(p.x[pi]);
+  const int ldx = p.ldx[pi];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // ty: rows, tx: tokens
+  const int nb = m_tile * 64, tb = n_tile * 64;
+  float acc[4][4] = {};
+  for (int kk = k0; kk < k1; kk += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int r = i >> 4, c = i & 15;
+      const int n = nb + r, t = tb + r, k = kk + c;
+      sW[c][r] = (n < P.Nw && k < k1) ? ld<T>(W + (size_t)n * P.K + k) : 0.f;
+      sX[c][r] = (t < P.T && k < k1) ? ld<T>(X + (size_t)t * ldx + k) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = sW[c][ty * 4 + i];
+        b[i] = sX[c][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int n = nb + ty * 4 + i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = tb + tx * 4 + j;
+      if (n >= P.Nw || t >= P.T) continue;
+      if (P.kind == EPI_GELU_UP) {
+        if (!(i & 1)) epi_gelu_pair<T>(P, n, t, acc[i][j], acc[i + 1][j]);
+      } else if (P.kind == EPI_ARGMAX) {
+        if (P.out) st<T>(reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n, acc[i][j]);
+        atomicMax(P.best + t, argmax_key<T>(acc[i][j], n));
+      } else {
+        epi_elem<T>(P, n, t, acc[i][j], split);
+      }
+    }
+  }
+}
+
+}  // namespace one

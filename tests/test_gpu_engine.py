@@ -1,0 +1,138 @@
+"""GPU parity of the decode engine (libone_b200.so through its C ABI) against the
+reference's own outputs (tests/golden/) and the CPU oracle.
+
+Tolerances: bf16 rtol = atol = 2e-2, fp32 rtol = atol = 1e-5 (logits, hx, cx)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cuda_ok
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")]
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+DT = {"fp32": torch.float32, "bf16": torch.bfloat16}
+TOL = {"fp32": dict(rtol=1e-5, atol=1e-5), "bf16": dict(rtol=2e-2, atol=2e-2)}
+
+
+def load(name):
+    return np.load(os.path.join(G, name))
+
+
+def tiny_sd(dt):
+    from one.configuration_one import tiny_config
+    from one.initialization import init_state_dict
+    cfg = tiny_config()
+    return cfg, {k: v.to(DT[dt]) for k, v in init_state_dict(cfg, 0, torch.float32).items()}
+
+
+def make_engine(cfg, sd, dt, **kw):
+    from one.engine import OneEngine
+    return OneEngine(cfg, sd, "cuda", DT[dt], **kw)
+
+
+def assert_close(a, b, dt, what):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    err = np.abs(a - b) - (TOL[dt]["atol"] + TOL[dt]["rtol"] * np.abs(b))
+    bad = err > 0
+    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} outside tolerance, max |diff| {np.abs(a - b).max():.3g}"
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+def test_forward_logits_and_state_match_reference(dt):
+    """Tiny model, ids [2, 64], every position (OneForCausalLM.forward, no cache)."""
+    g = load(f"forward_{dt}.npz")
+    cfg, sd = tiny_sd(dt)
+    eng = make_engine(cfg, sd, dt, max_batch=2, max_tokens=128)
+    ids = torch.from_numpy(g["ids"]).cuda()
+    lg = eng.prefill(ids, logits="all")
+    torch.cuda.synchronize()
+    assert eng.device_error() == (0, 0)
+    lg = lg.float().cpu()
+    assert_close(lg[..., :512].numpy(), g["logits_slice"], dt, "logits")
+    assert (lg.argmax(-1).numpy() == g["logits_argmax"]).mean() > 0.95
+    hx, cx = eng.last_hx_cx(128)
+    assert_close(hx.float().cpu().view(2, 64, -1).numpy(), g["hx"], dt, "hx")
+    assert_close(cx.float().cpu().view(2, 64, -1).numpy(), g["cx"], dt, "cx")
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+def test_cached_decode_matches_reference(dt):
+    """Prompt [3, 12], then 10 single-token steps fed the reference's tokens."""
+    g = load(f"decode_{dt}.npz")
+    cfg, sd = tiny_sd(dt)
+    eng = make_engine(cfg, sd, dt, max_batch=3, max_tokens=64)
+    eng.prefill(torch.from_numpy(g["prompt"]).cuda())
+    gen = torch.from_numpy(g["generated"]).cuda()
+    for s in range(gen.shape[1]):
+        lg, nxt = eng.step(gen[:, s], logits=True)
+        torch.cuda.synchronize()
+        assert_close(lg.float().cpu()[:, :512].numpy(), g["logits_slice"][s], dt, f"step {s} logits")
+        hx, cx = eng.last_hx_cx(3)
+        assert_close(hx.float().cpu().numpy(), g["step_hx"][s], dt, f"step {s} hx")
+        assert_close(cx.float().cpu().numpy(), g["step_cx"][s], dt, f"step {s} cx")
+    assert eng.device_error() == (0, 0)
+
+
+def test_greedy_decode_matches_reference_bf16():
+    """Autonomous greedy decode (argmax fed back on the device) reproduces the tokens."""
+    g = load("decode_bf16.npz")
+    cfg, sd = tiny_sd("bf16")
+    eng = make_engine(cfg, sd, "bf16", max_batch=3, max_tokens=64)
+    eng.prefill(torch.from_numpy(g["prompt"]).cuda())
+    steps = g["generated"].shape[1]
+    for _ in range(steps):
+        eng.step(None, next_ids=False)
+    torch.cuda.synchronize()
+    got = eng.history(steps, 3).cpu().numpy().T
+    assert (got == g["generated"]).mean() >= 0.9, (got, g["generated"])
+    assert eng.counters() == (12 + steps, steps)
+
+
+def test_140m_decode_matches_oracle_bf16():
+    """140M-class model, 4 sequences, prompt 8, 4 steps fed the oracle's greedy tokens."""
+    from one.configuration_one import config_140m
+    from one.initialization import init_state_dict
+    from oracle import one_oracle as O
+    from test_oracle_golden import ocfg
+    cfg = config_140m()
+    sd = init_state_dict(cfg, 4, torch.bfloat16)
+    prompt = torch.randint(0, 32000, (4, 8), generator=torch.Generator().manual_seed(4))
+    dec = O.RunningDecoder(sd, ocfg(cfg), torch.bfloat16)
+    gen, lgs, res = O.greedy(dec, prompt, 4, keep_logits=True)
+    eng = make_engine(cfg, sd, "bf16", max_batch=4, max_tokens=32)
+    eng.prefill(prompt.cuda())
+    for s in range(4):
+        lg, _ = eng.step(gen[:, s].cuda(), logits=True)
+        torch.cuda.synchronize()
+        assert_close(lg.float().cpu().numpy(), lgs[s].float().numpy(), "bf16", f"step {s} logits")
+    # running state equals the oracle's fp32 sums
+    st = eng.state()[:, :4].cpu()
+    for l in range(cfg.num_hidden_layers):
+        np.testing.assert_allclose(st[l].numpy(), dec.S[l].numpy(), rtol=2e-2, atol=2e-2)
+    assert eng.device_error() == (0, 0)
+
+
+def test_graph_replay_equals_stepwise():
+    """A captured multi-step greedy graph reproduces step-by-step greedy decode."""
+    from one.configuration_one import tiny_config
+    from one.initialization import init_state_dict
+    cfg = tiny_config()
+    sd = init_state_dict(cfg, 3, torch.bfloat16)
+    prompt = torch.randint(0, 32000, (5, 16), generator=torch.Generator().manual_seed(5)).cuda()
+    a = make_engine(cfg, sd, "bf16", max_batch=5, max_tokens=80)
+    a.prefill(prompt)
+    for _ in range(12):
+        a.step(None, next_ids=False)
+    b = make_engine(cfg, sd, "bf16", max_batch=5, max_tokens=80)
+    b.prefill(prompt)
+    b.capture(6)
+    b.replay()
+    b.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(a.history(12, 5), b.history(12, 5))
+    assert torch.equal(a.state()[:, :5], b.state()[:, :5])
+    assert a.counters() == b.counters() == (28, 12)
