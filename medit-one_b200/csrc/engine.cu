@@ -187,9 +187,13 @@ static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, Dev
   memset(&L.sg, 0, sizeof(L.sg));
   L.dtype = dtype;
   bool tc = dtype == ONE_DTYPE_BF16;
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   for (int i = 0; i < n && tc; ++i) {
     const ProbSpec& s = ps[i];
-    if ((reinterpret_cast<uintptr_t>(s.W) & 15) || (reinterpret_cast<uintptr_t>(s.X) & 15) || (s.K % 8) || (s.ldx % 8))
+    // TMA operands: 16-byte aligned rows; vector epilogue: 8-wide rows and chunks
+    if (!a16(s.W) || !a16(s.X) || (s.K % 8) || (s.ldx % 8) || (s.Nw % (s.kind == EPI_GELU_UP ? 16 : 8)) ||
+        !a16(s.out) || !a16(s.out2) || !a16(s.aux) || !a16(s.bias) || !a16(s.ws) || (s.ldo % 8) || (s.ldo2 % 8) ||
+        (s.lda % 8) || (s.ldw % 8))
       tc = false;
   }
   const int BN = tc ? pick_bn(T) : 64;
@@ -285,8 +289,10 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<128>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::kSmem));
   const int attn_max = 200 * 1024;
-  CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
-  CK(cudaFuncSetAttribute(row_attn_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
+  CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
+  CK(cudaFuncSetAttribute(row_attn_kernel<float, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
+  CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
+  CK(cudaFuncSetAttribute(row_attn_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(moe_router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(moe_router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   g_attrs_set = true;
@@ -295,12 +301,7 @@ static int set_kernel_attrs() {
 
 template <typename T>
 static cudaError_t launch_row_pre(const Launch& L, cudaStream_t st) {
-  switch (L.nv) {
-    case 1: return launch_k(row_pre_kernel<T, 1>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
-    case 2: return launch_k(row_pre_kernel<T, 2>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
-    case 3: return launch_k(row_pre_kernel<T, 3>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
-    default: return launch_k(row_pre_kernel<T, 4>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
-  }
+  return launch_k(row_pre_kernel<T>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
 }
 template <typename T>
 static cudaError_t launch_row_norm(const Launch& L, cudaStream_t st) {
@@ -331,8 +332,12 @@ static int run(const Launch& L, cudaStream_t st) {
     case L_ROW_PRE: e = bf ? launch_row_pre<__nv_bfloat16>(L, st) : launch_row_pre<float>(L, st); break;
     case L_ROW_NORM: e = bf ? launch_row_norm<__nv_bfloat16>(L, st) : launch_row_norm<float>(L, st); break;
     case L_ROW_ATTN:
-      e = bf ? launch_k(row_attn_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra)
-             : launch_k(row_attn_kernel<float>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra);
+      if (L.nv == 16)
+        e = bf ? launch_k(row_attn_kernel<__nv_bfloat16, 16>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra)
+               : launch_k(row_attn_kernel<float, 16>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra);
+      else
+        e = bf ? launch_k(row_attn_kernel<__nv_bfloat16, 64>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra)
+               : launch_k(row_attn_kernel<float, 64>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra);
       break;
     case L_SCAN:
       e = bf ? launch_k(scan_mean_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), 0, st, L.sc)
@@ -591,8 +596,8 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
     rp.kind = L_ROW_PRE;
     rp.dtype = dt;
     rp.nv = nv;
-    rp.block = 256;
-    rp.grid = (T + 7) / 8;
+    rp.block = ((D / 8 + 31) / 32) * 32;
+    rp.grid = T;
     RowPreParams& p = rp.rp;
     memset(&p, 0, sizeof(p));
     p.T = T;
@@ -662,9 +667,10 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       Launch a;
       a.kind = L_ROW_ATTN;
       a.dtype = dt;
-      a.block = 128;
+      a.block = kAttnThreads;
       a.grid = std::min(T, num_sms() * 4);
-      a.smem = row_attn_smem_bytes(H, Dh, std::max(c.r, 1));
+      a.smem = row_attn_smem_bytes(H, Dh, std::max(c.r, 1), D);
+      a.nv = H <= 16 ? 16 : 64;
       RowAttnParams& q = a.ra;
       memset(&q, 0, sizeof(q));
       q.T = T; q.H = H; q.Dh = Dh; q.r = c.r; q.E = c.num_experts; q.k = c.top_k; q.use_moe = moe ? 1 : 0;
@@ -760,8 +766,8 @@ static int build_final(one_engine* e, std::vector<Launch>& plan, int T, int batc
   rp.kind = L_ROW_PRE;
   rp.dtype = dt;
   rp.nv = nv;
-  rp.block = 256;
-  rp.grid = (T + 7) / 8;
+  rp.block = ((D / 8 + 31) / 32) * 32;
+  rp.grid = T;
   RowPreParams& p = rp.rp;
   memset(&p, 0, sizeof(p));
   p.T = T;

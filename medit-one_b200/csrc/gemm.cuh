@@ -134,6 +134,122 @@ ONE_DEVINL void epi_gelu_pair(const GemmProblem& P, int n_even, int t, float g, 
   st<T>(reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + (n_even >> 1), a * ub);
 }
 
+
+// E2 of the tensor-core epilogue (and the whole epilogue of nothing else): S holds the
+// fp32 accumulator of rows n_base .. n_base+127 for tokens t_base .. t_base+tn-1, laid
+// out S[t_local * 128 + n_local]. Rows >= Nw are padding. Requires Nw % 8 == 0 (16 for
+// GELU_UP), 8-aligned leading dimensions and 16-byte-aligned pointers (checked by the
+// planner).
+template <typename T>
+__device__ __forceinline__ void epilogue_tile(const GemmProblem& P, const float* S, int n_base, int t_base, int tn,
+                                              int split, int nthreads) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
+  if (tn <= 0) return;
+  if (P.kind == EPI_ARGMAX) {
+    T* out = reinterpret_cast<T*>(P.out);
+    for (int tl = warp; tl < tn; tl += nwarps) {
+      const int nl = lane * 4;
+      const float4 f = *reinterpret_cast<const float4*>(S + tl * 128 + nl);
+      const float v[4] = {f.x, f.y, f.z, f.w};
+      unsigned long long key = 0ull;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int n = n_base + nl + e;
+        if (n < P.Nw) {
+          const unsigned long long k2 = argmax_key<T>(v[e], n);
+          key = k2 > key ? k2 : key;
+          if (out) st<T>(out + (size_t)(t_base + tl) * P.ldo + n, v[e]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+        key = k2 > key ? k2 : key;
+      }
+      if (lane == 0 && key) atomicMax(P.best + t_base + tl, key);
+    }
+    return;
+  }
+  if (P.kind == EPI_GELU_UP) {
+    // 128 interleaved rows -> 64 output features; unit = (token, 8 outputs)
+    T* out = reinterpret_cast<T*>(P.out);
+    for (int u = tid; u < tn * 8; u += nthreads) {
+      const int tl = u >> 3, c = u & 7;
+      const int n0 = n_base + c * 16;
+      if (n0 >= P.Nw) continue;
+      const float* sv = S + tl * 128 + c * 16;
+      float g[16];
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(sv + i);
+        g[i] = f.x; g[i + 1] = f.y; g[i + 2] = f.z; g[i + 3] = f.w;
+      }
+      float b[16];
+      if (P.bias) {
+        load8(reinterpret_cast<const T*>(P.bias) + n0, b);
+        load8(reinterpret_cast<const T*>(P.bias) + n0 + 8, b + 8);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) b[i] = 0.f;
+      }
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float gb = rnd<T>(g[2 * j] + b[2 * j]);
+        const float ub = rnd<T>(g[2 * j + 1] + b[2 * j + 1]);
+        o[j] = rnd<T>(gelu_erf(gb)) * ub;
+      }
+      store8(out + (size_t)(t_base + tl) * P.ldo + (n0 >> 1), o);
+    }
+    return;
+  }
+  // STORE / HXPRE / XMOE / CX / PARTIAL: unit = (token, 8 rows)
+  for (int u = tid; u < tn * 16; u += nthreads) {
+    const int tl = u >> 4, c = u & 15;
+    const int n0 = n_base + c * 8;
+    if (n0 >= P.Nw) continue;
+    const int t = t_base + tl;
+    float a[8];
+    {
+      const float4 f0 = *reinterpret_cast<const float4*>(S + tl * 128 + c * 8);
+      const float4 f1 = *reinterpret_cast<const float4*>(S + tl * 128 + c * 8 + 4);
+      a[0] = f0.x; a[1] = f0.y; a[2] = f0.z; a[3] = f0.w; a[4] = f1.x; a[5] = f1.y; a[6] = f1.z; a[7] = f1.w;
+    }
+    if (P.kind == EPI_PARTIAL) {
+      store8(P.ws + ((size_t)split * P.T + t) * P.ldw + n0, a);
+      continue;
+    }
+    if (P.bias) {
+      float b[8];
+      load8(reinterpret_cast<const T*>(P.bias) + n0, b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[e] += b[e];
+    }
+    T* out = reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n0;
+    if (P.kind == EPI_STORE) {
+      store8(out, a);
+    } else if (P.kind == EPI_CX) {
+      float y[8], z[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        y[e] = rnd<T>(a[e]);
+        z[e] = fminf(fmaxf(y[e], -1e4f), 1e4f);
+      }
+      store8(out, y);
+      store8(reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0, z);
+    } else {  // HXPRE: aux + clamp(y); XMOE: aux * clamp(y)
+      float x[8], y[8];
+      load8(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float cl = fminf(fmaxf(rnd<T>(a[e]), -100.f), 100.f);
+        y[e] = P.kind == EPI_HXPRE ? x[e] + cl : x[e] * cl;
+      }
+      store8(out, y);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ tensor-core kernel
 template <int BN>
 struct TcCfg {
@@ -234,48 +350,32 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tc_kernel(const __grid_const
       }
       umma_commit(accb);
     }
-  } else {
-    // epilogue warps 2..5; TMEM lane quarter is fixed by warp id % 4
-    pdl_wait();
-    const int q = warp & 3;
-    const int n = m_tile * 128 + q * 32 + lane;
-    const bool nvalid = n < P.Nw;
+  }
+  // ---------------- epilogue
+  // E1: warps 2..5 (TMEM lane quarter = warp % 4) move the accumulator into a shared fp32
+  //     staging tile S[token][row] (BN x 128), reusing the pipeline buffers: every MMA,
+  //     and so every read of those buffers, has completed once accb fires.
+  // E2: all six warps apply the epilogue on 8-wide row vectors and store 16-byte chunks.
+  float* S = reinterpret_cast<float*>(smem);
+  pdl_wait();
+  if (warp >= 2) {
     const bool ok = mbar_wait(accb, 0, p.err, 3);
     tc_fence_after();
     if (ok) {
-      pdl_launch_dependents();
+      const int q = warp & 3;
       for (int c0 = 0; c0 < BN; c0 += 16) {
-        const int t0 = n_tile * BN + c0;
-        if (t0 >= P.T) break;  // warp-uniform
+        if (n_tile * BN + c0 >= P.T) break;  // warp-uniform
         float v[16];
         tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
         tmem_ld_wait();
-        const int tn = min(16, P.T - t0);
-        if (P.kind == EPI_GELU_UP) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
-            if (nvalid && !(n & 1) && j < tn) epi_gelu_pair<__nv_bfloat16>(P, n, t0 + j, v[j], other);
-          }
-        } else if (P.kind == EPI_ARGMAX) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            unsigned long long key = nvalid ? argmax_key<__nv_bfloat16>(v[j], n) : 0ull;
-            if (nvalid && P.out && j < tn)
-              st<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(P.out) + (size_t)(t0 + j) * P.ldo + n, v[j]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, key, o);
-              key = ok2 > key ? ok2 : key;
-            }
-            if (lane == 0 && j < tn && key) atomicMax(P.best + t0 + j, key);
-          }
-        } else if (nvalid) {
-          for (int j = 0; j < tn; ++j) epi_elem<__nv_bfloat16>(P, n, t0 + j, v[j], split);
-        }
+        for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
       }
     }
+    pdl_launch_dependents();
   }
+  __syncthreads();
+  epilogue_tile<__nv_bfloat16>(P, S, m_tile * 128, n_tile * BN, min(BN, P.T - n_tile * BN), split, C::kThreads);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -102,31 +102,70 @@ struct RowPreParams {
   DevErr* err;
 };
 
-template <typename T, int NV>
-__global__ void __launch_bounds__(256) row_pre_kernel(const RowPreParams p) {
+// Sum over the CTA: warp shuffle, then across warps through red[slot * 32 + warp].
+template <int N>
+ONE_DEVINL void block_sum(float (&v)[N], float* red, int slot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    v[i] = warp_sum(v[i]);
+    if (lane == 0) red[(slot + i) * 32 + warp] = v[i];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += red[(slot + i) * 32 + w];
+    v[i] = s;
+  }
+}
+
+// y = norm(x) for this thread's chunk, given the row's sum of squares.
+template <typename T>
+ONE_DEVINL void chunk_norm(const float* x, float ss, int D, float eps, const T* w, const T* b, int c, float* y) {
+  const float r = 1.0f / sqrtf(ss / (float)D + eps);
+  float wv[8], bv[8];
+  load8(w + c * 8, wv);
+  if (b) load8(b + c * 8, bv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float v = rnd<T>(wv[e] * rnd<T>(x[e] * r));
+    y[e] = b ? rnd<T>(v + bv[e]) : v;
+  }
+}
+
+ONE_DEVINL float sumsq8(const float* x) {
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s += x[e] * x[e];
+  return s;
+}
+
+// One CTA per token; thread c owns elements [8c, 8c+8) of the D-wide rows. Every global
+// load of the token is issued before the first reduction.
+template <typename T>
+__global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
+  __shared__ float red[4 * 32];
   pdl_wait();
-  const int warps = blockDim.x >> 5;
-  const int t = blockIdx.x * warps + (threadIdx.x >> 5);
-  if (t >= p.T) return;
-  const int lane = threadIdx.x & 31;
-  const int D = p.D, nch = D / 8;
-  const size_t row = (size_t)t * D;
-  float h[NV][8], a[NV][8], b[NV][8];
+  const int t = blockIdx.x;
+  const int c = threadIdx.x;
+  const int D = p.D;
+  const bool act = c < D / 8;
+  const size_t off = (size_t)t * D + (size_t)c * 8;
+  float h[8], a[8], b[8];
 
   if (p.mode == PRE_FIRST) {
-    int id;
-    if (p.ids_from_best) {
-      const unsigned long long key = p.best[t];
-      id = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
-    } else {
-      id = p.ids[t];
-    }
-    if (id < 0 || id >= p.vocab) {  // never gather outside the embedding table
-      if (lane == 0) set_err(p.err, ERR_BAD_ARG, 100);
-      id = 0;
-    }
-    __syncwarp();
-    if (lane == 0) {
+    __shared__ int sid;
+    if (threadIdx.x == 0) {
+      int id = p.ids_from_best ? 0 : p.ids[t];
+      if (p.ids_from_best) {
+        const unsigned long long key = p.best[t];
+        id = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
+      }
+      if (id < 0 || id >= p.vocab) {  // never gather outside the embedding table
+        set_err(p.err, ERR_BAD_ARG, 100);
+        id = 0;
+      }
       // this step's lm_head argmax accumulates into best[t] again
       p.best[t] = 0ull;
       if (p.ids_out) p.ids_out[t] = id;
@@ -134,83 +173,89 @@ __global__ void __launch_bounds__(256) row_pre_kernel(const RowPreParams p) {
         const int step = p.counters[1];
         if (step < p.hist_cap) p.hist[(size_t)step * p.T + t] = id;
       }
+      sid = id;
     }
-    warp_load_row<T, NV>(reinterpret_cast<const T*>(p.emb) + (size_t)id * D, nch, h);
-#pragma unroll
-    for (int j = 0; j < NV; ++j)
+    __syncthreads();
+    if (act) {
+      load8(reinterpret_cast<const T*>(p.emb) + (size_t)sid * D + c * 8, h);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        a[j][e] = 1.0f;
-        b[j][e] = fminf(fmaxf(h[j][e], -1e4f), 1e4f);
+        a[e] = 1.0f;
+        b[e] = fminf(fmaxf(h[e], -1e4f), 1e4f);
       }
-    warp_store_row<T, NV>(reinterpret_cast<T*>(p.hx) + row, nch, a);
-    warp_store_row<T, NV>(reinterpret_cast<T*>(p.cx) + row, nch, h);
-    warp_store_row<T, NV>(reinterpret_cast<T*>(p.cxc) + row, nch, b);
-  } else {
-    // finish the previous layer: out = norm(out0 + down_proj(...)) (:571-573), h += out (:793)
-    warp_load_row<T, NV>(reinterpret_cast<const T*>(p.out0) + row, nch, a);
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nch) {
-        float m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int s = 0; s < p.splits; ++s) {
-          float v[8];
-          load8(p.ws + ((size_t)s * p.T + t) * D + c * 8, v);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) m[e] += v[e];
-        }
-        if (p.down_b) {
-          float v[8];
-          load8(reinterpret_cast<const T*>(p.down_b) + c * 8, v);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) m[e] += v[e];
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a[j][e] = rnd<T>(a[j][e] + rnd<T>(m[e]));
-      }
+      store8(reinterpret_cast<T*>(p.hx) + off, a);
+      store8(reinterpret_cast<T*>(p.cx) + off, h);
+      store8(reinterpret_cast<T*>(p.cxc) + off, b);
     }
+  } else {
+    // finish the previous layer: out = norm(out0 + down_proj(...)) (:571-573), h += out (:793),
+    // hx = norm(hx + hx_moe) (:563-564)
+    float hp[8];
+    if (act) {
+      float m[8];
+      load8(reinterpret_cast<const T*>(p.out0) + off, a);
+      load8(reinterpret_cast<const T*>(p.h) + off, h);
+      load8(reinterpret_cast<const T*>(p.hx_pre) + off, hp);
+      load8(p.ws + off, m);
+      for (int s = 1; s < p.splits; ++s) {
+        float v[8];
+        load8(p.ws + (size_t)s * p.T * D + off, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m[e] += v[e];
+      }
+      if (p.down_b) {
+        float v[8];
+        load8(reinterpret_cast<const T*>(p.down_b) + c * 8, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m[e] += v[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[e] = rnd<T>(a[e] + rnd<T>(m[e]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[e] = h[e] = hp[e] = 0.f;
+    }
+    float ss[2] = {sumsq8(a), sumsq8(hp)};
+    block_sum<2>(ss, red, 0);
     const T* nw = reinterpret_cast<const T*>(p.prev_norm_w);
     const T* nb = reinterpret_cast<const T*>(p.prev_norm_b);
-    warp_rmsnorm<T, NV>(a, nch, nw, nb, 1e-6f, D, b);
-    warp_load_row<T, NV>(reinterpret_cast<const T*>(p.h) + row, nch, h);
+    if (act) {
+      chunk_norm<T>(a, ss[0], D, 1e-6f, nw, nb, c, b);
 #pragma unroll
-    for (int j = 0; j < NV; ++j)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) h[j][e] = rnd<T>(h[j][e] + b[j][e]);
-    // hx = norm(hx + hx_moe) (:563-564)
-    warp_load_row<T, NV>(reinterpret_cast<const T*>(p.hx_pre) + row, nch, a);
-    warp_rmsnorm<T, NV>(a, nch, nw, nb, 1e-6f, D, b);
-    warp_store_row<T, NV>(reinterpret_cast<T*>(p.hx) + row, nch, b);
+      for (int e = 0; e < 8; ++e) h[e] = rnd<T>(h[e] + b[e]);
+      chunk_norm<T>(hp, ss[1], D, 1e-6f, nw, nb, c, b);
+      store8(reinterpret_cast<T*>(p.hx) + off, b);
+      store8(reinterpret_cast<T*>(p.h) + off, h);
+    }
     if (p.mode == PRE_FINAL) {
-      warp_store_row<T, NV>(reinterpret_cast<T*>(p.h) + row, nch, h);
-      warp_rmsnorm<T, NV>(h, nch, reinterpret_cast<const T*>(p.lhs_w), reinterpret_cast<const T*>(p.lhs_b), p.lhs_eps, D, a);
-      warp_store_row<T, NV>(reinterpret_cast<T*>(p.hf) + row, nch, a);
+      float s3[1] = {act ? sumsq8(h) : 0.f};
+      block_sum<1>(s3, red, 2);
+      if (act) {
+        chunk_norm<T>(h, s3[0], D, p.lhs_eps, reinterpret_cast<const T*>(p.lhs_w), reinterpret_cast<const T*>(p.lhs_b), c, a);
+        store8(reinterpret_cast<T*>(p.hf) + off, a);
+      }
       return;
     }
   }
-  warp_store_row<T, NV>(reinterpret_cast<T*>(p.h) + row, nch, h);
+  if (p.mode == PRE_FIRST && act) store8(reinterpret_cast<T*>(p.h) + off, h);
   // norm_x = norm1(h) (:340); OneRMSNorm(dim) keeps eps = 1e-6 and has no bias
-  warp_rmsnorm<T, NV>(h, nch, reinterpret_cast<const T*>(p.norm1_w), (const T*)nullptr, 1e-6f, D, a);
-  warp_store_row<T, NV>(reinterpret_cast<T*>(p.norm_x) + row, nch, a);
+  float sr[8];
+  if (p.decode && act) load8(p.S + off, sr);
+  float s3[1] = {act ? sumsq8(h) : 0.f};
+  block_sum<1>(s3, red, 3);
+  if (!act) return;
+  chunk_norm<T>(h, s3[0], D, 1e-6f, reinterpret_cast<const T*>(p.norm1_w), (const T*)nullptr, c, a);
+  store8(reinterpret_cast<T*>(p.norm_x) + off, a);
   if (p.decode) {
     // running sum replaces cache.update + cumsum (:358-376); mean = sum / arange[-1] (:379-387)
     const float dv = p.div[p.counters[0]];
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nch) {
-        float s[8];
-        load8(p.S + row + c * 8, s);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          s[e] += a[j][e];
-          b[j][e] = rnd<T>(rnd<T>(s[e]) / dv);
-        }
-        store8(p.S + row + c * 8, s);
-      }
+    for (int e = 0; e < 8; ++e) {
+      sr[e] += a[e];
+      b[e] = rnd<T>(rnd<T>(sr[e]) / dv);
     }
-    warp_store_row<T, NV>(reinterpret_cast<T*>(p.mean) + row, nch, b);
+    store8(p.S + off, sr);
+    store8(reinterpret_cast<T*>(p.mean) + off, b);
   }
 }
 
@@ -386,113 +431,251 @@ __device__ void cta_router(int r, int E, int k, const MoeRouter& R, int t, const
   __syncthreads();
 }
 
-// Feature attention (one/modeling_one.py:390-556): per head, RoPE on single_x * scale
-// and on key, three Dh->H projections, softmax(q*k - max) in fp32, times v; then the
-// hx_moe / x_moe routers on the H*H outputs and the cx_moe router on cx.
-template <typename T>
-__global__ void __launch_bounds__(128) row_attn_kernel(const RowAttnParams p) {
+// Feature attention (one/modeling_one.py:390-556) and the three LinearMoE routers for
+// one token per CTA iteration (4 warps).
+//   phase A: warp w handles heads w, w+4, ...: RoPE on single_x * scale and on key
+//            (rotate_half), q/k/v = lin_q/k/v (Dh -> H, bias) as lane partial sums reduced
+//            across the warp, softmax(q*k - max) in fp32 over lanes j < H, o = w * v.
+//   phase B: gate logits of hx_moe / x_moe (threads 0..2r-1), softmax over r (a warp per
+//            router), expert factors 1 + silu(mean_r(g * e)) (a warp per router), the
+//            per-expert biased sums (all threads, exact fp64, rounded once), the top-k
+//            restatement (one thread per router) and the combine (all threads).
+constexpr int kAttnThreads = 128;
+
+template <typename T, int HMAX>
+__global__ void __launch_bounds__(kAttnThreads) row_attn_kernel(const RowAttnParams p) {
   extern __shared__ float sm[];
-  const int H = p.H, Dh = p.Dh, HD = H * Dh, HH = H * H;
-  float* sx = sm;                 // [HD] single_x * scale
-  float* sk = sx + HD;            // [HD] key
-  float* sv = sk + HD;            // [HD] value
-  float* sxr = sv + HD;           // [HD] RoPE(single_x)
-  float* skr = sxr + HD;          // [HD] RoPE(key)
-  float* qkv = skr + HD;          // [3][HH]
-  float* so = qkv + 3 * HH;       // [HH]
-  float* cs = so + HH;            // [Dh] cos, [Dh] sin
-  float* gl = cs + 2 * Dh;        // [r]
-  float* cvals = gl + p.r;        // [E]
-  float* score = cvals + kMaxExperts;     // [E]
-  float* xs = score + kMaxExperts;        // router input, up to max(HH, D)
-  int* sel = reinterpret_cast<int*>(xs + 4096);
-  double* red = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(sel + kMaxExperts) + 7) & ~uintptr_t(7));  // [warps*8]
-  pdl_wait();
-  const int tid = threadIdx.x, nt = blockDim.x;
+  const int H = p.H, Dh = p.Dh, HD = H * Dh, HH = H * H, r = p.r, E = p.E;
+  const int D = p.rt[2].in;
+  float* wqkv = sm;                     // [3][H][Dh] lin_q / lin_k / lin_v weights
+  float* row = wqkv + 3 * H * Dh;       // [3][HD]: single_x * scale, key, value
+  float* cs = row + 3 * HD;             // [2][Dh] cos, sin
+  float* o = cs + 2 * Dh;               // [HH] attention output
+  float* xs = o + HH;                   // [HH] clamp(o)
+  float* cxs = xs + HH;                 // [D] clamp(cx)
+  float* gl = cxs + D;                  // [3][r] gate softmax
+  float* cv = gl + 3 * r;               // [3][kMaxExperts] 1 + silu(score)
+  float* sc = cv + 3 * kMaxExperts;     // [3][kMaxExperts] routing scores
+  int* sel = reinterpret_cast<int*>(sc + 3 * kMaxExperts);  // [3][kMaxExperts]
+  double* red = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(sel + 3 * kMaxExperts) + 7) & ~uintptr_t(7));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int half = Dh / 2;
+
+  // weights of the three head projections, once per CTA (they are not written by the
+  // previous kernel, so this runs before the dependency wait)
+  for (int i = tid; i < 3 * H * Dh; i += kAttnThreads) {
+    const int which = i / (H * Dh), rem = i % (H * Dh);
+    const T* W = reinterpret_cast<const T*>(which == 0 ? p.wq : which == 1 ? p.wk : p.wv);
+    wqkv[i] = ld<T>(W + rem);
+  }
+  pdl_wait();
+
   for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
     const int pos = p.counters[0] + (p.seq_len > 0 ? t % p.seq_len : 0);
-    // cos/sin (OneRotaryEmbedding, :159-182): fp32 freq = inv_freq * pos, cast to dtype
-    for (int i = tid; i < half; i += nt) {
+    // cos / sin (OneRotaryEmbedding, :159-182): fp32 inv_freq * pos, cast to the dtype
+    for (int i = tid; i < half; i += kAttnThreads) {
       const float f = p.inv_freq[i] * (float)pos;
       const float c = rnd<T>(cosf(f)), s = rnd<T>(sinf(f));
       cs[i] = c; cs[i + half] = c;
       cs[Dh + i] = s; cs[Dh + i + half] = s;
     }
     const T* pr = reinterpret_cast<const T*>(p.proj) + (size_t)t * 3 * HD;
-    for (int i = tid; i < HD; i += nt) {
-      sx[i] = rnd<T>(ld<T>(pr + i) * p.attn_scale);  // :405
-      sk[i] = ld<T>(pr + HD + i);
-      sv[i] = ld<T>(pr + 2 * HD + i);
+    for (int i = tid * 8; i < 3 * HD; i += kAttnThreads * 8) {
+      float v[8];
+      load8(pr + i, v);
+      if (i < HD)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = rnd<T>(v[e] * p.attn_scale);  // :405
+#pragma unroll
+      for (int e = 0; e < 8; ++e) row[i + e] = v[e];
+    }
+    if (p.use_moe) {
+      const T* X = reinterpret_cast<const T*>(p.rt[2].x) + (size_t)t * p.rt[2].ldx;
+      for (int i = tid * 8; i < D; i += kAttnThreads * 8) {
+        float v[8];
+        load8(X + i, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) cxs[i + e] = v[e];
+      }
     }
     __syncthreads();
-    // rotate_half RoPE (one/flash_attention.py:20-33): x*cos + rotate_half(x)*sin
-    for (int i = tid; i < HD; i += nt) {
-      const int d = i % Dh, base = i - d;
-      const float px = d < half ? -sx[base + d + half] : sx[base + d - half];
-      const float pk = d < half ? -sk[base + d + half] : sk[base + d - half];
-      sxr[i] = rnd<T>(rnd<T>(sx[i] * cs[d]) + rnd<T>(px * cs[Dh + d]));
-      skr[i] = rnd<T>(rnd<T>(sk[i] * cs[d]) + rnd<T>(pk * cs[Dh + d]));
-    }
-    __syncthreads();
-    // q = lin_q(xr), k = lin_k(kr), v = lin_v(value): Dh -> H per head, with bias
-    for (int w = tid; w < 3 * HH; w += nt) {
-      const int which = w / HH, hj = w % HH, h = hj / H, j = hj % H;
-      const T* W = reinterpret_cast<const T*>(which == 0 ? p.wq : which == 1 ? p.wk : p.wv);
-      const T* Bb = reinterpret_cast<const T*>(which == 0 ? p.bq : which == 1 ? p.bk : p.bv);
-      const float* src = (which == 0 ? sxr : which == 1 ? skr : sv) + h * Dh;
-      float acc = 0.f;
-      for (int d = 0; d < Dh; ++d) acc = fmaf(ld<T>(W + j * Dh + d), src[d], acc);
-      qkv[which * HH + hj] = rnd<T>(acc + ld<T>(Bb + j));
-    }
-    __syncthreads();
-    // softmax(q*k - max) in fp32, cast, NaN -> 1/H, times v (:530-547)
-    for (int h = tid; h < H; h += nt) {
-      float lg[64];
-      float mx = -INFINITY;
-      for (int j = 0; j < H; ++j) {
-        lg[j] = rnd<T>(qkv[h * H + j] * qkv[HH + h * H + j]);
-        mx = fmaxf(mx, lg[j]);
+
+    // ---- phase A: one warp per head
+    for (int h = warp; h < H; h += kAttnThreads / 32) {
+      const float* sx = row + h * Dh;
+      const float* sk = row + HD + h * Dh;
+      const float* sv = row + 2 * HD + h * Dh;
+      float pq[HMAX], pk_[HMAX], pv[HMAX];  // partial dot products, j < H <= HMAX
+#pragma unroll
+      for (int j = 0; j < HMAX; ++j) pq[j] = pk_[j] = pv[j] = 0.f;
+      for (int d = lane; d < Dh; d += 32) {
+        const float px = d < half ? -sx[d + half] : sx[d - half];
+        const float pk = d < half ? -sk[d + half] : sk[d - half];
+        const float xr = rnd<T>(rnd<T>(sx[d] * cs[d]) + rnd<T>(px * cs[Dh + d]));
+        const float kr = rnd<T>(rnd<T>(sk[d] * cs[d]) + rnd<T>(pk * cs[Dh + d]));
+        const float vv = sv[d];
+#pragma unroll
+        for (int j = 0; j < HMAX; ++j) {
+          if (j < H) {
+            pq[j] = fmaf(wqkv[j * Dh + d], xr, pq[j]);
+            pk_[j] = fmaf(wqkv[H * Dh + j * Dh + d], kr, pk_[j]);
+            pv[j] = fmaf(wqkv[2 * H * Dh + j * Dh + d], vv, pv[j]);
+          }
+        }
       }
-      float m2 = -INFINITY;
-      for (int j = 0; j < H; ++j) {
-        lg[j] = rnd<T>(lg[j] - mx);
-        m2 = fmaxf(m2, lg[j]);
+#pragma unroll
+      for (int j = 0; j < HMAX; ++j) {
+        if (j < H) {
+          pq[j] = warp_sum(pq[j]);
+          pk_[j] = warp_sum(pk_[j]);
+          pv[j] = warp_sum(pv[j]);
+        }
       }
-      float sum = 0.f;
-      for (int j = 0; j < H; ++j) {
-        lg[j] = expf(lg[j] - m2);
-        sum += lg[j];
+      float q = 0.f, k = 0.f, v = 0.f, lg = -INFINITY;
+      if (lane < H) {
+        // select this lane's j from the reduced values without dynamic register indexing
+#pragma unroll
+        for (int j = 0; j < HMAX; ++j)
+          if (j == lane) {
+            q = pq[j];
+            k = pk_[j];
+            v = pv[j];
+          }
+        q = rnd<T>(q + ld<T>(reinterpret_cast<const T*>(p.bq) + lane));
+        k = rnd<T>(k + ld<T>(reinterpret_cast<const T*>(p.bk) + lane));
+        v = rnd<T>(v + ld<T>(reinterpret_cast<const T*>(p.bv) + lane));
+        lg = rnd<T>(q * k);
       }
-      const float inv = 1.0f / sum;
-      for (int j = 0; j < H; ++j) {
-        float w = lg[j] * inv;
+      const float mx = warp_max(lg);
+      const float d1 = lane < H ? rnd<T>(lg - mx) : -INFINITY;
+      const float m2 = warp_max(d1);
+      const float ex = lane < H ? expf(d1 - m2) : 0.f;
+      const float sum = warp_sum(ex);
+      if (lane < H) {
+        float w = ex * (1.0f / sum);
         w = isnan(w) ? 1.0f / (float)H : rnd<T>(w);
-        so[h * H + j] = rnd<T>(w * qkv[2 * HH + h * H + j]);
+        o[h * H + lane] = rnd<T>(w * v);
       }
     }
     __syncthreads();
     if (p.o) {
       T* O = reinterpret_cast<T*>(p.o) + (size_t)t * HH;
-      for (int i = tid; i < HH; i += nt) st<T>(O + i, so[i]);
+      for (int i = tid; i < HH; i += kAttnThreads) st<T>(O + i, o[i]);
     }
-    if (p.use_moe) {
-      // hx_moe and x_moe route the same attention output, clamped to +-1e4 (:53)
-      for (int i = tid; i < HH; i += nt) xs[i] = fminf(fmaxf(so[i], -1e4f), 1e4f);
+    if (!p.use_moe) {
       __syncthreads();
-      cta_router<T>(p.r, p.E, p.k, p.rt[0], t, xs, gl, cvals, red, score, sel);
-      cta_router<T>(p.r, p.E, p.k, p.rt[1], t, xs, gl, cvals, red, score, sel);
-      // cx_moe routes clamp(cx), with gate logits from the projection GEMM
-      const MoeRouter& R = p.rt[2];
-      const T* X = reinterpret_cast<const T*>(R.x) + (size_t)t * R.ldx;
-      for (int i = tid; i < R.in; i += nt) xs[i] = ld<T>(X + i);
-      __syncthreads();
-      cta_router<T>(p.r, p.E, p.k, R, t, xs, gl, cvals, red, score, sel);
+      continue;
+    }
+    // ---- phase B: routers. xs = clamp(o) feeds hx_moe and x_moe (:53)
+    for (int i = tid; i < HH; i += kAttnThreads) xs[i] = fminf(fmaxf(o[i], -1e4f), 1e4f);
+    __syncthreads();
+    // gate logits (:56): hx (router 0) and x (router 1) from their gate weights; cx (2)
+    // precomputed by the projection GEMM
+    for (int j = tid; j < 2 * r; j += kAttnThreads) {
+      const int ri = j / r, jj = j % r;
+      const T* W = reinterpret_cast<const T*>(p.rt[ri].gate_w) + (size_t)jj * HH;
+      float acc = 0.f;
+      if ((HH & 7) == 0) {
+        for (int i = 0; i < HH; i += 8) {
+          float w8[8];
+          load8(W + i, w8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = fmaf(w8[e], xs[i + e], acc);
+        }
+      } else {
+        for (int i = 0; i < HH; ++i) acc = fmaf(ld<T>(W + i), xs[i], acc);
+      }
+      gl[ri * r + jj] = rnd<T>(acc);
+    }
+    {
+      const T* G = reinterpret_cast<const T*>(p.rt[2].glog) + (size_t)t * r;
+      for (int j = tid; j < r; j += kAttnThreads) gl[2 * r + j] = ld<T>(G + j);
+    }
+    __syncthreads();
+    // softmax over r, then the expert factors: one warp per router
+    if (warp < 3) {
+      float* g = gl + warp * r;
+      float mx = -INFINITY;
+      for (int j = lane; j < r; j += 32) mx = fmaxf(mx, g[j]);
+      mx = warp_max(mx);
+      float sum = 0.f;
+      for (int j = lane; j < r; j += 32) sum += expf(g[j] - mx);
+      sum = warp_sum(sum);
+      const float inv = 1.0f / sum;
+      __syncwarp();
+      for (int j = lane; j < r; j += 32) g[j] = rnd<T>(expf(g[j] - mx) * inv);
+      __syncwarp();
+      const T* EX = reinterpret_cast<const T*>(p.rt[warp].experts);
+      for (int e = 0; e < E; ++e) {
+        const float exv = fminf(fmaxf(ld<T>(EX + e), -10.f), 10.f);
+        double acc = 0.0;
+        for (int j = lane; j < r; j += 32) acc += (double)rnd<T>(g[j] * exv);
+        acc = warp_sum_d(acc);
+        if (lane == 0) {
+          const float scv = fminf(fmaxf(rnd<T>((float)acc / (float)r), -10.f), 10.f);
+          cv[warp * kMaxExperts + e] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
+        }
+      }
+    }
+    __syncthreads();
+    // per-expert sums of x * c_e + bias2[e] (:71-80): exact fp64 sums, rounded once
+    for (int ri = 0; ri < 3; ++ri) {
+      const float* x = ri < 2 ? xs : cxs;
+      const int in = ri < 2 ? HH : D;
+      const T* B2 = reinterpret_cast<const T*>(p.rt[ri].bias2);
+      const float* c = cv + ri * kMaxExperts;
+      for (int e0 = 0; e0 < E; e0 += 8) {
+        double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int i = tid; i < in; i += kAttnThreads) {
+          const float xi = x[i];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e0 + e < E) acc[e] += (double)rnd<T>(rnd<T>(xi * c[e0 + e]) + ld<T>(B2 + (size_t)(e0 + e) * in + i));
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
+        if (lane == 0)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) red[warp * 8 + e] = acc[e];
+        __syncthreads();
+        if (tid < 8 && e0 + tid < E) {
+          double s = 0.0;
+          for (int w = 0; w < kAttnThreads / 32; ++w) s += red[w * 8 + tid];
+          sc[ri * kMaxExperts + e0 + tid] = rnd<T>(__double2float_rn(s));
+        }
+        __syncthreads();
+      }
+    }
+    // top-k (:83-84): one thread per router
+    const int kk = min(p.k, E);
+    if (lane == 0 && warp < 3) {
+      int chosen[kMaxExperts];
+      topk_select(sc + warp * kMaxExperts, E, kk, chosen);
+      for (int j = 0; j < kk; ++j) {
+        sel[warp * kMaxExperts + j] = chosen[j];
+        if (p.rt[warp].idx_out) p.rt[warp].idx_out[(size_t)t * kk + j] = chosen[j];
+      }
+    }
+    __syncthreads();
+    // combine: mean of the selected biased inputs (:87-90), fp32 sum in selection order
+    for (int ri = 0; ri < 3; ++ri) {
+      const float* x = ri < 2 ? xs : cxs;
+      const int in = ri < 2 ? HH : D;
+      const T* B2 = reinterpret_cast<const T*>(p.rt[ri].bias2);
+      const float* c = cv + ri * kMaxExperts;
+      T* Cm = reinterpret_cast<T*>(p.rt[ri].comb) + (size_t)t * in;
+      for (int i = tid; i < in; i += kAttnThreads) {
+        float s = 0.f;
+        for (int j = 0; j < kk; ++j) {
+          const int e = sel[ri * kMaxExperts + j];
+          s += rnd<T>(rnd<T>(x[i] * c[e]) + ld<T>(B2 + (size_t)e * in + i));
+        }
+        st<T>(Cm + i, s / (float)kk);
+      }
     }
     __syncthreads();
   }
 }
-
 
 // LinearMoE router alone (standalone op): per token, clamp the input (:53), then the
 // router of cta_router. gate logits come precomputed in R.glog.
@@ -518,12 +701,10 @@ inline size_t moe_router_smem_bytes(int in, int r) {
   return (size_t)(in + r + 2 * kMaxExperts) * 4 + (kMaxExperts + 2) * 4 + 8 + 4 * 8 * 8;
 }
 
-inline size_t row_attn_smem_bytes(int H, int Dh, int r) {
-  const int HD = H * Dh, HH = H * H;
-  size_t f = (size_t)5 * HD + 4 * HH + 2 * Dh + r + 2 * kMaxExperts + 4096;
-  size_t bytes = f * 4 + kMaxExperts * 4;
-  bytes = (bytes + 7) & ~(size_t)7;
-  return bytes + 8 + 4 * 8 * 8;  // align slack + warps * 8 doubles
+inline size_t row_attn_smem_bytes(int H, int Dh, int r, int D) {
+  const size_t HD = (size_t)H * Dh, HH = (size_t)H * H;
+  size_t f = 3 * HD + 3 * HD + 2 * (size_t)Dh + 2 * HH + (size_t)D + 3 * (size_t)r + 6 * kMaxExperts;
+  return f * 4 + 3 * kMaxExperts * 4 + 8 + 4 * 8 * 8;
 }
 
 }  // namespace one

@@ -109,10 +109,10 @@ def test_140m_decode_matches_oracle_bf16():
         lg, _ = eng.step(gen[:, s].cuda(), logits=True)
         torch.cuda.synchronize()
         assert_close(lg.float().cpu().numpy(), lgs[s].float().numpy(), "bf16", f"step {s} logits")
-    # running state equals the oracle's fp32 sums
+    # running state: the mean the model consumes (S / P, P = 12 tokens) matches the oracle's
     st = eng.state()[:, :4].cpu()
     for l in range(cfg.num_hidden_layers):
-        np.testing.assert_allclose(st[l].numpy(), dec.S[l].numpy(), rtol=2e-2, atol=2e-2)
+        assert_close(st[l].numpy() / 12.0, dec.S[l].numpy() / 12.0, "bf16", f"layer {l} running mean")
     assert eng.device_error() == (0, 0)
 
 
