@@ -122,6 +122,10 @@ void* one_engine_buffer(one_engine* e, const char* name);
 int one_engine_error(one_engine* e, int32_t* code, int32_t* where);
 /* Number of kernels one_engine_step launches for `batch` sequences. */
 int32_t one_engine_step_launches(one_engine* e, int32_t batch);
+/* Time each launch of one decode step separately (reps back-to-back runs between two
+ * CUDA events on `stream`, warm caches): us_out[i] = mean microseconds of launch i.
+ * Returns the number of launches written (<= n), or -1. Advances the decode state. */
+int32_t one_engine_profile_step(one_engine* e, int32_t batch, int32_t reps, float* us_out, int32_t n, void* stream);
 
 /* ------------------------------------------------------------------ standalone ops */
 

@@ -173,11 +173,16 @@ static int num_sms() {
   return g_num_sms;
 }
 
-static int pick_bn(int T) {
+// Token-tile width: enough CTAs to cover the SMs twice where possible, wider tiles
+// (fewer weight re-reads from L2) when the problem already has many weight tiles.
+static int pick_bn(int T, int m_tiles_total) {
   if (T >= 8192) return 256;
   if (T >= 2048) return 128;
-  if (T > 32) return 64;
-  return 32;
+  for (int bn : {256, 128, 64}) {
+    const int ctas = m_tiles_total * ((T + bn - 1) / bn);
+    if (bn <= T * 2 && ctas >= 2 * num_sms()) return bn;
+  }
+  return T > 32 ? 64 : 32;
 }
 
 // Build one GEMM launch over up to four independent problems sharing T tokens.
@@ -196,7 +201,9 @@ static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, Dev
         (s.lda % 8) || (s.ldw % 8))
       tc = false;
   }
-  const int BN = tc ? pick_bn(T) : 64;
+  int mt_total = 0;
+  for (int i = 0; i < n; ++i) mt_total += (ps[i].Nw + 127) / 128;
+  const int BN = tc ? pick_bn(T, mt_total) : 64;
   const int BM = tc ? 128 : 64;
   L.kind = tc ? L_GEMM_TC : L_GEMM_SIMT;
   L.bn = BN;
@@ -614,6 +621,7 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
     p.counters = counters;
     p.emb = e->gw[ONE_G_EMBED];
     p.div = e->ddiv;
+    p.div_len = e->div_len;
     p.ws = e->at<float>(e->b.ws);
     p.out0 = B_(e->b.out0);
     p.hx_pre = B_(e->b.hx_pre);
@@ -667,10 +675,13 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       Launch a;
       a.kind = L_ROW_ATTN;
       a.dtype = dt;
-      a.block = kAttnThreads;
+      a.block = 32 * std::max(4, std::min(H, kAttnMaxThreads / 32));
       a.grid = std::min(T, num_sms() * 4);
-      a.smem = row_attn_smem_bytes(H, Dh, std::max(c.r, 1), D);
       a.nv = H <= 16 ? 16 : 64;
+      a.smem = attn_layout(H, Dh, c.r, c.num_experts, D, a.block, moe ? 1 : 0, es).total;
+      if (a.smem > 200 * 1024) return fail(ONE_ERR_UNSUPPORTED, "attention/router weights exceed shared memory (%zu B)", a.smem);
+      if (moe && (HH % 8 || D % 8 || (c.r * HH) % 8 || D > 8 * 256))
+        return fail(ONE_ERR_UNSUPPORTED, "router shapes: H*H and D must be multiples of 8, D <= 2048");
       RowAttnParams& q = a.ra;
       memset(&q, 0, sizeof(q));
       q.T = T; q.H = H; q.Dh = Dh; q.r = c.r; q.E = c.num_experts; q.k = c.top_k; q.use_moe = moe ? 1 : 0;
@@ -964,6 +975,35 @@ extern "C" int one_engine_error(one_engine* e, int32_t* code, int32_t* where) {
   if (code) *code = h.code;
   if (where) *where = h.where;
   return h.code != 0;
+}
+
+// Time every launch of a decode step separately: each launch runs `reps` times back to
+// back between two CUDA events on `stream`; us_out[i] is the mean duration of launch i
+// (warm caches). Returns the number of launches (<= n) or -1.
+extern "C" int32_t one_engine_profile_step(one_engine* e, int32_t batch, int32_t reps, float* us_out, int32_t n,
+                                           void* stream) {
+  if (!e || batch < 1 || batch > e->max_batch || reps < 1 || !us_out) return -1;
+  std::vector<Launch> plan;
+  if (build_step(e, plan, batch, nullptr, nullptr, nullptr)) return -1;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaEvent_t a, b;
+  if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) return -1;
+  const int m = std::min<int>(n, (int)plan.size());
+  for (int i = 0; i < (int)plan.size(); ++i) {
+    if (i < m) cudaEventRecord(a, st);
+    for (int r = 0; r < (i < m ? reps : 1); ++r)
+      if (run(plan[i], st)) return -1;
+    if (i < m) {
+      cudaEventRecord(b, st);
+      cudaEventSynchronize(b);
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, a, b);
+      us_out[i] = 1000.f * ms / reps;
+    }
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  return m;
 }
 
 #include "capi_ops.cuh"

@@ -253,10 +253,16 @@ __device__ __forceinline__ void epilogue_tile(const GemmProblem& P, const float*
 // ------------------------------------------------------------------ tensor-core kernel
 template <int BN>
 struct TcCfg {
-  static constexpr int kStages = BN >= 256 ? 3 : 4;
+  // pipeline depth that keeps two CTAs per SM (<= ~100 KB of stages)
+  static constexpr int kStages = BN >= 256 ? 2 : (BN >= 128 ? 3 : 4);
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = BN * 64 * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  // the epilogue stages the accumulator through the (drained) pipeline buffers in
+  // column chunks of kChunk tokens: kChunk * 128 rows * 4 B must fit in them
+  static constexpr int kChunk = (kStages * kStageBytes) / (128 * 4) >= BN ? BN : 128;
+  static_assert(kChunk * 128 * 4 <= kStages * kStageBytes, "epilogue staging tile exceeds the pipeline buffers");
+  static_assert(BN % kChunk == 0, "token tile must be a multiple of the staging chunk");
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr int kThreads = 192;  // w0 TMA, w1 MMA + TMEM owner, w2..5 epilogue
 };
@@ -307,6 +313,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) pdl_launch_dependents();
 
   auto sA = [&](int s) { return smem + s * C::kStageBytes; };
   auto sB = [&](int s) { return smem + s * C::kStageBytes + C::kABytes; };
@@ -358,24 +365,28 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tc_kernel(const __grid_const
   // E2: all six warps apply the epilogue on 8-wide row vectors and store 16-byte chunks.
   float* S = reinterpret_cast<float*>(smem);
   pdl_wait();
+  bool ok = true;
   if (warp >= 2) {
-    const bool ok = mbar_wait(accb, 0, p.err, 3);
+    ok = mbar_wait(accb, 0, p.err, 3);
     tc_fence_after();
-    if (ok) {
+  }
+  for (int cc = 0; cc < BN; cc += C::kChunk) {
+    if (warp >= 2 && ok) {
       const int q = warp & 3;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (n_tile * BN + c0 >= P.T) break;  // warp-uniform
+      for (int c0 = 0; c0 < C::kChunk; c0 += 16) {
+        if (n_tile * BN + cc + c0 >= P.T) break;  // warp-uniform
         float v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc + c0), v);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
       }
     }
-    pdl_launch_dependents();
+    __syncthreads();
+    const int t_base = n_tile * BN + cc;
+    epilogue_tile<__nv_bfloat16>(P, S, m_tile * 128, t_base, min(C::kChunk, P.T - t_base), split, C::kThreads);
+    __syncthreads();
   }
-  __syncthreads();
-  epilogue_tile<__nv_bfloat16>(P, S, m_tile * 128, n_tile * BN, min(BN, P.T - n_tile * BN), split, C::kThreads);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

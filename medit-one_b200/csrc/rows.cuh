@@ -78,6 +78,7 @@ struct RowPreParams {
   const int* counters;    // {pos, step}
   const void* emb;        // [V, D]
   const float* div;       // divisor per position (decode)
+  int div_len;
   // previous layer's tail
   const float* ws;        // [splits][T][D] down_proj partials
   int splits;
@@ -146,6 +147,7 @@ ONE_DEVINL float sumsq8(const float* x) {
 template <typename T>
 __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
   __shared__ float red[4 * 32];
+  pdl_launch_dependents();
   pdl_wait();
   const int t = blockIdx.x;
   const int c = threadIdx.x;
@@ -248,7 +250,12 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
   store8(reinterpret_cast<T*>(p.norm_x) + off, a);
   if (p.decode) {
     // running sum replaces cache.update + cumsum (:358-376); mean = sum / arange[-1] (:379-387)
-    const float dv = p.div[p.counters[0]];
+    int pi = p.counters[0];
+    if (pi >= p.div_len) {  // position beyond the divisor table the engine was built with
+      if (threadIdx.x == 0) set_err(p.err, ERR_BAD_ARG, 101);
+      pi = p.div_len - 1;
+    }
+    const float dv = p.div[pi];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       sr[e] += a[e];
@@ -272,6 +279,7 @@ struct ScanParams {
 
 template <typename T>
 __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
+  pdl_launch_dependents();
   pdl_wait();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= p.B * p.D) return;
@@ -301,6 +309,7 @@ struct RowNormParams {
 
 template <typename T, int NV>
 __global__ void __launch_bounds__(256) row_norm_kernel(const RowNormParams p) {
+  pdl_launch_dependents();
   pdl_wait();
   if (p.counters && blockIdx.x == 0 && threadIdx.x == 0) {
     p.counters[0] += 1;
@@ -431,56 +440,133 @@ __device__ void cta_router(int r, int E, int k, const MoeRouter& R, int t, const
   __syncthreads();
 }
 
+// Shared-memory layout of row_attn_kernel (byte offsets), shared by host and device.
+struct AttnLayout {
+  int wqkv, bqkv, gate, gate_ld, experts, b2, row, cs, rot, qkv, o, xs, cxs, gl, gpart, cv, cpart, red, sc, sel, total;
+};
+__host__ __device__ inline int attn_take(int& off, int bytes) {
+  const int o = off;
+  off = (off + bytes + 15) & ~15;
+  return o;
+}
+__host__ __device__ inline AttnLayout attn_layout(int H, int Dh, int r, int E, int D, int nthreads, int use_moe, int es) {
+  AttnLayout L;
+  int off = 0;
+  const int HD = H * Dh, HH = H * H, nw = nthreads / 32;
+  L.wqkv = attn_take(off, 3 * H * (Dh + 1) * 4);
+  L.bqkv = attn_take(off, 3 * H * 4);
+  L.gate_ld = HH + (es == 2 ? 2 : 1);  // odd row stride in 32-bit words: conflict-free rows
+  L.gate = attn_take(off, use_moe ? 2 * r * L.gate_ld * es : 0);
+  L.experts = attn_take(off, use_moe ? 3 * E * 4 : 0);
+  L.b2 = attn_take(off, use_moe ? E * (2 * HH + D) * es : 0);
+  L.row = attn_take(off, 3 * HD * 4);
+  L.cs = attn_take(off, 2 * Dh * 4);
+  L.rot = attn_take(off, H * 2 * Dh * 4);
+  L.qkv = attn_take(off, H * 3 * H * 4);
+  L.o = attn_take(off, HH * 4);
+  L.xs = attn_take(off, HH * 4);
+  L.cxs = attn_take(off, use_moe ? D * 4 : 0);
+  L.gl = attn_take(off, 3 * r * 4);
+  L.gpart = attn_take(off, 4 * 2 * r * 4);
+  L.cv = attn_take(off, 3 * E * 4);
+  L.cpart = attn_take(off, 3 * 32 * 8);
+  L.red = attn_take(off, 3 * kMaxExperts * 8 * 8);  // [router][expert][chunk] partial sums
+  L.sc = attn_take(off, 3 * E * 4);
+  L.sel = attn_take(off, 3 * E * 4);
+  L.total = off;
+  return L;
+}
+
 // Feature attention (one/modeling_one.py:390-556) and the three LinearMoE routers for
-// one token per CTA iteration (4 warps).
-//   phase A: warp w handles heads w, w+4, ...: RoPE on single_x * scale and on key
-//            (rotate_half), q/k/v = lin_q/k/v (Dh -> H, bias) as lane partial sums reduced
-//            across the warp, softmax(q*k - max) in fp32 over lanes j < H, o = w * v.
-//   phase B: gate logits of hx_moe / x_moe (threads 0..2r-1), softmax over r (a warp per
-//            router), expert factors 1 + silu(mean_r(g * e)) (a warp per router), the
-//            per-expert biased sums (all threads, exact fp64, rounded once), the top-k
-//            restatement (one thread per router) and the combine (all threads).
-constexpr int kAttnThreads = 128;
+// one token per CTA iteration. Every weight the kernel reads (lin_q/k/v, the hx_moe /
+// x_moe gates, experts, bias2) is copied to shared memory before the dependency wait.
+//   phase A : warp per head: RoPE (rotate_half) on single_x * scale and on key into
+//             shared rows, then lane u computes projection output u of q|k|v (Dh -> H,
+//             bias, rounded), then softmax(q*k - max) in fp32 over lanes j < H, o = w*v.
+//   phase B : gate logits of hx_moe / x_moe (all threads, split dot products), softmax
+//             over r and expert factors 1 + silu(mean_r(g * e)) (a warp per router), the
+//             per-expert biased sums of all three routers in one pass (exact fp64, rounded
+//             once), the top-k restatement (a thread per router) and the combine.
+constexpr int kAttnMaxThreads = 384;
 
 template <typename T, int HMAX>
-__global__ void __launch_bounds__(kAttnThreads) row_attn_kernel(const RowAttnParams p) {
-  extern __shared__ float sm[];
+__global__ void __launch_bounds__(kAttnMaxThreads, 2) row_attn_kernel(const RowAttnParams p) {
+  extern __shared__ __align__(16) uint8_t smb[];
   const int H = p.H, Dh = p.Dh, HD = H * Dh, HH = H * H, r = p.r, E = p.E;
-  const int D = p.rt[2].in;
-  float* wqkv = sm;                     // [3][H][Dh] lin_q / lin_k / lin_v weights
-  float* row = wqkv + 3 * H * Dh;       // [3][HD]: single_x * scale, key, value
-  float* cs = row + 3 * HD;             // [2][Dh] cos, sin
-  float* o = cs + 2 * Dh;               // [HH] attention output
-  float* xs = o + HH;                   // [HH] clamp(o)
-  float* cxs = xs + HH;                 // [D] clamp(cx)
-  float* gl = cxs + D;                  // [3][r] gate softmax
-  float* cv = gl + 3 * r;               // [3][kMaxExperts] 1 + silu(score)
-  float* sc = cv + 3 * kMaxExperts;     // [3][kMaxExperts] routing scores
-  int* sel = reinterpret_cast<int*>(sc + 3 * kMaxExperts);  // [3][kMaxExperts]
-  double* red = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(sel + 3 * kMaxExperts) + 7) & ~uintptr_t(7));
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int half = Dh / 2;
+  const int D = p.use_moe ? p.rt[2].in : 0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nw = nthr >> 5;
+  const AttnLayout L = attn_layout(H, Dh, r, E, D, nthr, p.use_moe, (int)sizeof(T));
+  float* wqkv = reinterpret_cast<float*>(smb + L.wqkv);
+  float* bqkv = reinterpret_cast<float*>(smb + L.bqkv);
+  T* gate = reinterpret_cast<T*>(smb + L.gate);
+  float* exps = reinterpret_cast<float*>(smb + L.experts);
+  T* b2s = reinterpret_cast<T*>(smb + L.b2);
+  float* row = reinterpret_cast<float*>(smb + L.row);
+  float* cs = reinterpret_cast<float*>(smb + L.cs);
+  float* rot = reinterpret_cast<float*>(smb + L.rot);
+  float* qkv = reinterpret_cast<float*>(smb + L.qkv);
+  float* o = reinterpret_cast<float*>(smb + L.o);
+  float* xs = reinterpret_cast<float*>(smb + L.xs);
+  float* cxs = reinterpret_cast<float*>(smb + L.cxs);
+  float* gl = reinterpret_cast<float*>(smb + L.gl);
+  float* gpart = reinterpret_cast<float*>(smb + L.gpart);
+  float* cv = reinterpret_cast<float*>(smb + L.cv);
+  double* cpart = reinterpret_cast<double*>(smb + L.cpart);
+  double* red = reinterpret_cast<double*>(smb + L.red);
+  float* sc = reinterpret_cast<float*>(smb + L.sc);
+  int* sel = reinterpret_cast<int*>(smb + L.sel);
+  const int half = Dh / 2, Dp = Dh + 1;
+  const int inr[3] = {HH, HH, D};
+  const int b2off[3] = {0, E * HH, 2 * E * HH};
 
-  // weights of the three head projections, once per CTA (they are not written by the
-  // previous kernel, so this runs before the dependency wait)
-  for (int i = tid; i < 3 * H * Dh; i += kAttnThreads) {
-    const int which = i / (H * Dh), rem = i % (H * Dh);
+  // ---- weights to shared memory (not written by the previous kernel: before the wait),
+  // copied as 16-byte vectors
+  constexpr int VE = 16 / (int)sizeof(T);  // elements per 16-byte vector
+  for (int v = tid; v < 3 * HD / 8; v += nthr) {
+    const int u = (v * 8) / Dh, d0 = (v * 8) % Dh, which = u / H;
     const T* W = reinterpret_cast<const T*>(which == 0 ? p.wq : which == 1 ? p.wk : p.wv);
-    wqkv[i] = ld<T>(W + rem);
+    float x[8];
+    load8(W + (size_t)(u % H) * Dh + d0, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) wqkv[u * Dp + d0 + e] = x[e];
   }
+  for (int i = tid; i < 3 * H; i += nthr) {
+    const int which = i / H, j = i % H;
+    const T* Bb = reinterpret_cast<const T*>(which == 0 ? p.bq : which == 1 ? p.bk : p.bv);
+    bqkv[i] = ld<T>(Bb + j);
+  }
+  if (p.use_moe) {
+    {
+      // 32-bit copies into rows of gate_ld elements (an odd number of words)
+      const int wpr = HH * (int)sizeof(T) / 4, wld = L.gate_ld * (int)sizeof(T) / 4;
+      for (int w = tid; w < 2 * r * wpr; w += nthr) {
+        const int j = w / wpr, c = w % wpr, ri = j / r;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.rt[ri].gate_w);
+        reinterpret_cast<uint32_t*>(gate)[j * wld + c] = src[(j % r) * wpr + c];
+      }
+    }
+    for (int ri = 0; ri < 3; ++ri) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.rt[ri].bias2);
+      uint4* dst = reinterpret_cast<uint4*>(b2s + b2off[ri]);
+      for (int v = tid; v < E * inr[ri] / VE; v += nthr) dst[v] = src[v];
+    }
+    for (int i = tid; i < 3 * E; i += nthr)
+      exps[i] = fminf(fmaxf(ld<T>(reinterpret_cast<const T*>(p.rt[i / E].experts) + i % E), -10.f), 10.f);
+  }
+  if (tid == 0) pdl_launch_dependents();
   pdl_wait();
 
   for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
     const int pos = p.counters[0] + (p.seq_len > 0 ? t % p.seq_len : 0);
     // cos / sin (OneRotaryEmbedding, :159-182): fp32 inv_freq * pos, cast to the dtype
-    for (int i = tid; i < half; i += kAttnThreads) {
+    for (int i = tid; i < half; i += nthr) {
       const float f = p.inv_freq[i] * (float)pos;
-      const float c = rnd<T>(cosf(f)), s = rnd<T>(sinf(f));
+      const float c = rnd<T>(cosf(f)), sn = rnd<T>(sinf(f));
       cs[i] = c; cs[i + half] = c;
-      cs[Dh + i] = s; cs[Dh + i + half] = s;
+      cs[Dh + i] = sn; cs[Dh + i + half] = sn;
     }
     const T* pr = reinterpret_cast<const T*>(p.proj) + (size_t)t * 3 * HD;
-    for (int i = tid * 8; i < 3 * HD; i += kAttnThreads * 8) {
+    for (int i = tid * 8; i < 3 * HD; i += nthr * 8) {
       float v[8];
       load8(pr + i, v);
       if (i < HD)
@@ -491,60 +577,45 @@ __global__ void __launch_bounds__(kAttnThreads) row_attn_kernel(const RowAttnPar
     }
     if (p.use_moe) {
       const T* X = reinterpret_cast<const T*>(p.rt[2].x) + (size_t)t * p.rt[2].ldx;
-      for (int i = tid * 8; i < D; i += kAttnThreads * 8) {
+      for (int i = tid * 8; i < D; i += nthr * 8) {
         float v[8];
         load8(X + i, v);
 #pragma unroll
         for (int e = 0; e < 8; ++e) cxs[i + e] = v[e];
       }
+      const T* G = reinterpret_cast<const T*>(p.rt[2].glog) + (size_t)t * r;
+      for (int j = tid; j < r; j += nthr) gl[2 * r + j] = ld<T>(G + j);
     }
     __syncthreads();
 
     // ---- phase A: one warp per head
-    for (int h = warp; h < H; h += kAttnThreads / 32) {
+    for (int h = warp; h < H; h += nw) {
       const float* sx = row + h * Dh;
       const float* sk = row + HD + h * Dh;
       const float* sv = row + 2 * HD + h * Dh;
-      float pq[HMAX], pk_[HMAX], pv[HMAX];  // partial dot products, j < H <= HMAX
-#pragma unroll
-      for (int j = 0; j < HMAX; ++j) pq[j] = pk_[j] = pv[j] = 0.f;
+      float* xr = rot + h * 2 * Dh;
+      float* kr = xr + Dh;
       for (int d = lane; d < Dh; d += 32) {
         const float px = d < half ? -sx[d + half] : sx[d - half];
         const float pk = d < half ? -sk[d + half] : sk[d - half];
-        const float xr = rnd<T>(rnd<T>(sx[d] * cs[d]) + rnd<T>(px * cs[Dh + d]));
-        const float kr = rnd<T>(rnd<T>(sk[d] * cs[d]) + rnd<T>(pk * cs[Dh + d]));
-        const float vv = sv[d];
-#pragma unroll
-        for (int j = 0; j < HMAX; ++j) {
-          if (j < H) {
-            pq[j] = fmaf(wqkv[j * Dh + d], xr, pq[j]);
-            pk_[j] = fmaf(wqkv[H * Dh + j * Dh + d], kr, pk_[j]);
-            pv[j] = fmaf(wqkv[2 * H * Dh + j * Dh + d], vv, pv[j]);
-          }
-        }
+        xr[d] = rnd<T>(rnd<T>(sx[d] * cs[d]) + rnd<T>(px * cs[Dh + d]));
+        kr[d] = rnd<T>(rnd<T>(sk[d] * cs[d]) + rnd<T>(pk * cs[Dh + d]));
       }
-#pragma unroll
-      for (int j = 0; j < HMAX; ++j) {
-        if (j < H) {
-          pq[j] = warp_sum(pq[j]);
-          pk_[j] = warp_sum(pk_[j]);
-          pv[j] = warp_sum(pv[j]);
-        }
+      __syncwarp();
+      float* qh = qkv + h * 3 * H;
+      for (int u = lane; u < 3 * H; u += 32) {
+        const int which = u / H;
+        const float* src = which == 0 ? xr : which == 1 ? kr : sv;
+        const float* w = wqkv + u * Dp;
+        float acc = 0.f;
+        for (int d = 0; d < Dh; ++d) acc = fmaf(w[d], src[d], acc);
+        qh[u] = rnd<T>(acc + bqkv[u]);
       }
-      float q = 0.f, k = 0.f, v = 0.f, lg = -INFINITY;
+      __syncwarp();
+      float lg = -INFINITY, v = 0.f;
       if (lane < H) {
-        // select this lane's j from the reduced values without dynamic register indexing
-#pragma unroll
-        for (int j = 0; j < HMAX; ++j)
-          if (j == lane) {
-            q = pq[j];
-            k = pk_[j];
-            v = pv[j];
-          }
-        q = rnd<T>(q + ld<T>(reinterpret_cast<const T*>(p.bq) + lane));
-        k = rnd<T>(k + ld<T>(reinterpret_cast<const T*>(p.bk) + lane));
-        v = rnd<T>(v + ld<T>(reinterpret_cast<const T*>(p.bv) + lane));
-        lg = rnd<T>(q * k);
+        lg = rnd<T>(qh[lane] * qh[H + lane]);
+        v = qh[2 * H + lane];
       }
       const float mx = warp_max(lg);
       const float d1 = lane < H ? rnd<T>(lg - mx) : -INFINITY;
@@ -554,45 +625,43 @@ __global__ void __launch_bounds__(kAttnThreads) row_attn_kernel(const RowAttnPar
       if (lane < H) {
         float w = ex * (1.0f / sum);
         w = isnan(w) ? 1.0f / (float)H : rnd<T>(w);
-        o[h * H + lane] = rnd<T>(w * v);
+        const float ov = rnd<T>(w * v);
+        o[h * H + lane] = ov;
+        xs[h * H + lane] = fminf(fmaxf(ov, -1e4f), 1e4f);  // LinearMoE input clamp (:53)
       }
     }
     __syncthreads();
     if (p.o) {
       T* O = reinterpret_cast<T*>(p.o) + (size_t)t * HH;
-      for (int i = tid; i < HH; i += kAttnThreads) st<T>(O + i, o[i]);
+      for (int i = tid; i < HH; i += nthr) st<T>(O + i, o[i]);
     }
     if (!p.use_moe) {
       __syncthreads();
       continue;
     }
-    // ---- phase B: routers. xs = clamp(o) feeds hx_moe and x_moe (:53)
-    for (int i = tid; i < HH; i += kAttnThreads) xs[i] = fminf(fmaxf(o[i], -1e4f), 1e4f);
-    __syncthreads();
-    // gate logits (:56): hx (router 0) and x (router 1) from their gate weights; cx (2)
-    // precomputed by the projection GEMM
-    for (int j = tid; j < 2 * r; j += kAttnThreads) {
-      const int ri = j / r, jj = j % r;
-      const T* W = reinterpret_cast<const T*>(p.rt[ri].gate_w) + (size_t)jj * HH;
-      float acc = 0.f;
-      if ((HH & 7) == 0) {
-        for (int i = 0; i < HH; i += 8) {
-          float w8[8];
-          load8(W + i, w8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(w8[e], xs[i + e], acc);
-        }
-      } else {
-        for (int i = 0; i < HH; ++i) acc = fmaf(ld<T>(W + i), xs[i], acc);
-      }
-      gl[ri * r + jj] = rnd<T>(acc);
-    }
+    // ---- phase B1: gate logits of hx_moe / x_moe (:56) on clamp(o) (:53): a thread per
+    // (gate row, slice of the row), partial sums added in slice order
     {
-      const T* G = reinterpret_cast<const T*>(p.rt[2].glog) + (size_t)t * r;
-      for (int j = tid; j < r; j += kAttnThreads) gl[2 * r + j] = ld<T>(G + j);
+      const int n2 = 2 * r;
+      const int parts = max(1, min(nthr / n2, 4));
+      const int chunk = (HH + parts - 1) / parts;
+      for (int w = tid; w < n2 * parts; w += nthr) {
+        const int j = w % n2, part = w / n2;
+        const T* Wg = gate + j * L.gate_ld;
+        const int i0 = part * chunk, i1 = min(HH, i0 + chunk);
+        float acc = 0.f;
+        for (int i = i0; i < i1; ++i) acc = fmaf(ld<T>(Wg + i), xs[i], acc);
+        gpart[part * n2 + j] = acc;
+      }
+      __syncthreads();
+      for (int j = tid; j < n2; j += nthr) {
+        float acc = 0.f;
+        for (int part = 0; part < parts; ++part) acc += gpart[part * n2 + j];
+        gl[j] = rnd<T>(acc);
+      }
     }
     __syncthreads();
-    // softmax over r, then the expert factors: one warp per router
+    // ---- phase B2: softmax over r and the expert factors, one warp per router
     if (warp < 3) {
       float* g = gl + warp * r;
       float mx = -INFINITY;
@@ -605,72 +674,87 @@ __global__ void __launch_bounds__(kAttnThreads) row_attn_kernel(const RowAttnPar
       __syncwarp();
       for (int j = lane; j < r; j += 32) g[j] = rnd<T>(expf(g[j] - mx) * inv);
       __syncwarp();
-      const T* EX = reinterpret_cast<const T*>(p.rt[warp].experts);
-      for (int e = 0; e < E; ++e) {
-        const float exv = fminf(fmaxf(ld<T>(EX + e), -10.f), 10.f);
+      // mean over r of rnd(g * e): lanes split as (expert e, slice); exact fp64 partial sums
+      const float* ex = exps + warp * E;
+      double* cp = cpart + warp * 32;
+      for (int e0 = 0; e0 < E; e0 += 32) {
+        const int ne = min(32, E - e0);
+        const int slices = 32 / ne;
+        const int e = lane % ne, sl = lane / ne;
         double acc = 0.0;
-        for (int j = lane; j < r; j += 32) acc += (double)rnd<T>(g[j] * exv);
-        acc = warp_sum_d(acc);
-        if (lane == 0) {
-          const float scv = fminf(fmaxf(rnd<T>((float)acc / (float)r), -10.f), 10.f);
-          cv[warp * kMaxExperts + e] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
+        if (sl < slices)
+          for (int j = sl; j < r; j += slices) acc += (double)rnd<T>(g[j] * ex[e0 + e]);
+        cp[lane] = acc;
+        __syncwarp();
+        if (lane < ne) {
+          double s2 = 0.0;
+          for (int q = 0; q < slices; ++q) s2 += cp[q * ne + lane];
+          const float scv = fminf(fmaxf(rnd<T>((float)s2 / (float)r), -10.f), 10.f);
+          cv[warp * E + e0 + lane] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
         }
+        __syncwarp();
       }
     }
     __syncthreads();
-    // per-expert sums of x * c_e + bias2[e] (:71-80): exact fp64 sums, rounded once
-    for (int ri = 0; ri < 3; ++ri) {
-      const float* x = ri < 2 ? xs : cxs;
-      const int in = ri < 2 ? HH : D;
-      const T* B2 = reinterpret_cast<const T*>(p.rt[ri].bias2);
-      const float* c = cv + ri * kMaxExperts;
-      for (int e0 = 0; e0 < E; e0 += 8) {
-        double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int i = tid; i < in; i += kAttnThreads) {
-          const float xi = x[i];
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (e0 + e < E) acc[e] += (double)rnd<T>(rnd<T>(xi * c[e0 + e]) + ld<T>(B2 + (size_t)(e0 + e) * in + i));
+    // ---- phase B3: per-expert sums of x * c_e + bias2[e] (:71-80) for the three routers:
+    // a warp per (router, expert, 256-element chunk), exact fp64 sums, rounded once
+    {
+      constexpr int CH = 256;
+      const int nch[3] = {(HH + CH - 1) / CH, (HH + CH - 1) / CH, (D + CH - 1) / CH};
+      const int items = E * (nch[0] + nch[1] + nch[2]);
+      for (int it = warp; it < items; it += nw) {
+        int ri = 0, rem = it;
+        while (rem >= E * nch[ri]) { rem -= E * nch[ri]; ++ri; }
+        const int e = rem / nch[ri], ch = rem % nch[ri];
+        const int in = inr[ri];
+        const float* x = ri < 2 ? xs : cxs;
+        const T* B2 = b2s + b2off[ri] + (size_t)e * in;
+        const float c = cv[ri * E + e];
+        double acc = 0.0;
+        const int i1 = min(in, (ch + 1) * CH);
+        if (c == 1.0f) {
+          for (int i = ch * CH + lane; i < i1; i += 32) acc += (double)rnd<T>(x[i] + ld<T>(B2 + i));
+        } else {
+          for (int i = ch * CH + lane; i < i1; i += 32) acc += (double)rnd<T>(rnd<T>(x[i] * c) + ld<T>(B2 + i));
         }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
-        if (lane == 0)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) red[warp * 8 + e] = acc[e];
-        __syncthreads();
-        if (tid < 8 && e0 + tid < E) {
-          double s = 0.0;
-          for (int w = 0; w < kAttnThreads / 32; ++w) s += red[w * 8 + tid];
-          sc[ri * kMaxExperts + e0 + tid] = rnd<T>(__double2float_rn(s));
-        }
-        __syncthreads();
+        acc = warp_sum_d(acc);
+        if (lane == 0) red[(ri * kMaxExperts + e) * 8 + ch] = acc;
       }
+      __syncthreads();
+      for (int q = tid; q < 3 * E; q += nthr) {
+        const int ri = q / E, e = q % E;
+        double s2 = 0.0;
+        for (int ch = 0; ch < nch[ri]; ++ch) s2 += red[(ri * kMaxExperts + e) * 8 + ch];
+        sc[ri * E + e] = rnd<T>(__double2float_rn(s2));
+      }
+      __syncthreads();
     }
-    // top-k (:83-84): one thread per router
+    // ---- phase B4: top-k (:83-84), a thread per router
     const int kk = min(p.k, E);
     if (lane == 0 && warp < 3) {
       int chosen[kMaxExperts];
-      topk_select(sc + warp * kMaxExperts, E, kk, chosen);
+      topk_select(sc + warp * E, E, kk, chosen);
       for (int j = 0; j < kk; ++j) {
-        sel[warp * kMaxExperts + j] = chosen[j];
+        sel[warp * E + j] = chosen[j];
         if (p.rt[warp].idx_out) p.rt[warp].idx_out[(size_t)t * kk + j] = chosen[j];
       }
     }
     __syncthreads();
-    // combine: mean of the selected biased inputs (:87-90), fp32 sum in selection order
-    for (int ri = 0; ri < 3; ++ri) {
-      const float* x = ri < 2 ? xs : cxs;
-      const int in = ri < 2 ? HH : D;
-      const T* B2 = reinterpret_cast<const T*>(p.rt[ri].bias2);
-      const float* c = cv + ri * kMaxExperts;
-      T* Cm = reinterpret_cast<T*>(p.rt[ri].comb) + (size_t)t * in;
-      for (int i = tid; i < in; i += kAttnThreads) {
-        float s = 0.f;
+    // ---- phase B5: combine, the mean of the selected biased inputs (:87-90)
+    {
+      const int ntot = 2 * HH + D;
+      for (int g = tid; g < ntot; g += nthr) {
+        const int ri = g < HH ? 0 : (g < 2 * HH ? 1 : 2);
+        const int i = ri == 0 ? g : (ri == 1 ? g - HH : g - 2 * HH);
+        const float xi = ri < 2 ? xs[i] : cxs[i];
+        const T* B2 = b2s + b2off[ri];
+        const float* c = cv + ri * E;
+        float s2 = 0.f;
         for (int j = 0; j < kk; ++j) {
-          const int e = sel[ri * kMaxExperts + j];
-          s += rnd<T>(rnd<T>(x[i] * c[e]) + ld<T>(B2 + (size_t)e * in + i));
+          const int e = sel[ri * E + j];
+          s2 += rnd<T>(rnd<T>(xi * c[e]) + ld<T>(B2 + (size_t)e * inr[ri] + i));
         }
-        st<T>(Cm + i, s / (float)kk);
+        st<T>(reinterpret_cast<T*>(p.rt[ri].comb) + (size_t)t * inr[ri] + i, s2 / (float)kk);
       }
     }
     __syncthreads();
@@ -701,10 +785,5 @@ inline size_t moe_router_smem_bytes(int in, int r) {
   return (size_t)(in + r + 2 * kMaxExperts) * 4 + (kMaxExperts + 2) * 4 + 8 + 4 * 8 * 8;
 }
 
-inline size_t row_attn_smem_bytes(int H, int Dh, int r, int D) {
-  const size_t HD = (size_t)H * Dh, HH = (size_t)H * H;
-  size_t f = 3 * HD + 3 * HD + 2 * (size_t)Dh + 2 * HH + (size_t)D + 3 * (size_t)r + 6 * kMaxExperts;
-  return f * 4 + 3 * kMaxExperts * 4 + 8 + 4 * 8 * 8;
-}
 
 }  // namespace one

@@ -13,105 +13,143 @@ namespace one {
 
 constexpr int kMaxExperts = 64;
 
-struct TopkQ {
+// Queue in (local) memory: any n <= kMaxExperts.
+struct TopkMemQ {
   float v[kMaxExperts];
   int i[kMaxExperts];
+  ONE_DEVINL float gv(int j) const { return v[j]; }
+  ONE_DEVINL int gi(int j) const { return i[j]; }
+  ONE_DEVINL void set(int j, float x, int ix) { v[j] = x; i[j] = ix; }
+};
+// Queue in registers for n <= N: every access is an unrolled select over N slots.
+template <int N>
+struct TopkRegQ {
+  float v[N];
+  int i[N];
+  ONE_DEVINL float gv(int j) const {
+    float r = v[0];
+#pragma unroll
+    for (int k = 1; k < N; ++k) r = (j == k) ? v[k] : r;
+    return r;
+  }
+  ONE_DEVINL int gi(int j) const {
+    int r = i[0];
+#pragma unroll
+    for (int k = 1; k < N; ++k) r = (j == k) ? i[k] : r;
+    return r;
+  }
+  ONE_DEVINL void set(int j, float x, int ix) {
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+      if (j == k) { v[k] = x; i[k] = ix; }
+  }
 };
 
 ONE_DEVINL bool tk_gt(float a, float b) {
   const bool an = isnan(a), bn = isnan(b);
   return (an && !bn) || (a > b);
 }
-ONE_DEVINL void tk_swap(TopkQ& q, int a, int b) {
-  float tv = q.v[a]; q.v[a] = q.v[b]; q.v[b] = tv;
-  int ti = q.i[a]; q.i[a] = q.i[b]; q.i[b] = ti;
+template <class Q>
+ONE_DEVINL void tk_swap(Q& q, int a, int b) {
+  const float va = q.gv(a), vb = q.gv(b);
+  const int ia = q.gi(a), ib = q.gi(b);
+  q.set(a, vb, ib);
+  q.set(b, va, ia);
 }
-ONE_DEVINL void tk_insertion_sort(TopkQ& q, int lo, int hi) {
+template <class Q>
+ONE_DEVINL void tk_insertion_sort(Q& q, int lo, int hi) {
   for (int i = lo + 1; i < hi; ++i) {
-    const float v = q.v[i];
-    const int ix = q.i[i];
-    if (tk_gt(v, q.v[lo])) {
-      for (int j = i; j > lo; --j) { q.v[j] = q.v[j - 1]; q.i[j] = q.i[j - 1]; }
-      q.v[lo] = v; q.i[lo] = ix;
+    const float v = q.gv(i);
+    const int ix = q.gi(i);
+    if (tk_gt(v, q.gv(lo))) {
+      for (int j = i; j > lo; --j) q.set(j, q.gv(j - 1), q.gi(j - 1));
+      q.set(lo, v, ix);
     } else {
       int j = i;
-      while (tk_gt(v, q.v[j - 1])) { q.v[j] = q.v[j - 1]; q.i[j] = q.i[j - 1]; --j; }
-      q.v[j] = v; q.i[j] = ix;
+      while (tk_gt(v, q.gv(j - 1))) {
+        q.set(j, q.gv(j - 1), q.gi(j - 1));
+        --j;
+      }
+      q.set(j, v, ix);
     }
   }
 }
-ONE_DEVINL void tk_median_to_first(TopkQ& q, int r, int a, int b, int c) {
-  if (tk_gt(q.v[a], q.v[b])) {
-    if (tk_gt(q.v[b], q.v[c])) tk_swap(q, r, b);
-    else if (tk_gt(q.v[a], q.v[c])) tk_swap(q, r, c);
+template <class Q>
+ONE_DEVINL void tk_median_to_first(Q& q, int r, int a, int b, int c) {
+  if (tk_gt(q.gv(a), q.gv(b))) {
+    if (tk_gt(q.gv(b), q.gv(c))) tk_swap(q, r, b);
+    else if (tk_gt(q.gv(a), q.gv(c))) tk_swap(q, r, c);
     else tk_swap(q, r, a);
-  } else if (tk_gt(q.v[a], q.v[c])) tk_swap(q, r, a);
-  else if (tk_gt(q.v[b], q.v[c])) tk_swap(q, r, c);
+  } else if (tk_gt(q.gv(a), q.gv(c))) tk_swap(q, r, a);
+  else if (tk_gt(q.gv(b), q.gv(c))) tk_swap(q, r, c);
   else tk_swap(q, r, b);
 }
-ONE_DEVINL int tk_partition(TopkQ& q, int first, int last, int pivot) {
+template <class Q>
+ONE_DEVINL int tk_partition(Q& q, int first, int last, int pivot) {
+  const float pv = q.gv(pivot);  // the pivot slot is outside [first, last): never moved here
   while (true) {
-    while (tk_gt(q.v[first], q.v[pivot])) ++first;
+    while (tk_gt(q.gv(first), pv)) ++first;
     --last;
-    while (tk_gt(q.v[pivot], q.v[last])) --last;
+    while (tk_gt(pv, q.gv(last))) --last;
     if (!(first < last)) return first;
     tk_swap(q, first, last);
     ++first;
   }
 }
 // libstdc++ __adjust_heap followed by __push_heap, on q[first .. first+len)
-ONE_DEVINL void tk_adjust_heap(TopkQ& q, int first, int hole, int len, float val, int vix) {
+template <class Q>
+ONE_DEVINL void tk_adjust_heap(Q& q, int first, int hole, int len, float val, int vix) {
   const int top = hole;
   int second = hole;
   while (second < (len - 1) / 2) {
     second = 2 * (second + 1);
-    if (tk_gt(q.v[first + second], q.v[first + second - 1])) --second;
-    q.v[first + hole] = q.v[first + second]; q.i[first + hole] = q.i[first + second];
+    if (tk_gt(q.gv(first + second), q.gv(first + second - 1))) --second;
+    q.set(first + hole, q.gv(first + second), q.gi(first + second));
     hole = second;
   }
   if ((len & 1) == 0 && second == (len - 2) / 2) {
     second = 2 * (second + 1);
-    q.v[first + hole] = q.v[first + second - 1]; q.i[first + hole] = q.i[first + second - 1];
+    q.set(first + hole, q.gv(first + second - 1), q.gi(first + second - 1));
     hole = second - 1;
   }
   int parent = (hole - 1) / 2;
-  while (hole > top && tk_gt(q.v[first + parent], val)) {
-    q.v[first + hole] = q.v[first + parent]; q.i[first + hole] = q.i[first + parent];
+  while (hole > top && tk_gt(q.gv(first + parent), val)) {
+    q.set(first + hole, q.gv(first + parent), q.gi(first + parent));
     hole = parent;
     parent = (hole - 1) / 2;
   }
-  q.v[first + hole] = val; q.i[first + hole] = vix;
+  q.set(first + hole, val, vix);
 }
-ONE_DEVINL void tk_heap_select(TopkQ& q, int first, int middle, int last) {
+template <class Q>
+ONE_DEVINL void tk_heap_select(Q& q, int first, int middle, int last) {
   const int len = middle - first;
   if (len >= 2)
     for (int parent = (len - 2) / 2;; --parent) {
-      tk_adjust_heap(q, first, parent, len, q.v[first + parent], q.i[first + parent]);
+      tk_adjust_heap(q, first, parent, len, q.gv(first + parent), q.gi(first + parent));
       if (parent == 0) break;
     }
   for (int i = middle; i < last; ++i)
-    if (tk_gt(q.v[i], q.v[first])) {
-      const float v = q.v[i];
-      const int ix = q.i[i];
-      q.v[i] = q.v[first]; q.i[i] = q.i[first];
+    if (tk_gt(q.gv(i), q.gv(first))) {
+      const float v = q.gv(i);
+      const int ix = q.gi(i);
+      q.set(i, q.gv(first), q.gi(first));
       tk_adjust_heap(q, first, 0, len, v, ix);
     }
 }
-ONE_DEVINL void tk_sort_heap(TopkQ& q, int first, int last) {
+template <class Q>
+ONE_DEVINL void tk_sort_heap(Q& q, int first, int last) {
   while (last - first > 1) {
     --last;
-    const float v = q.v[last];
-    const int ix = q.i[last];
-    q.v[last] = q.v[first]; q.i[last] = q.i[first];
+    const float v = q.gv(last);
+    const int ix = q.gi(last);
+    q.set(last, q.gv(first), q.gi(first));
     tk_adjust_heap(q, first, 0, last - first, v, ix);
   }
 }
 ONE_DEVINL int tk_lg(int n) { return 31 - __clz(n); }
 
-// Select k of n scores; writes the chosen indices, in the reference's order, to out[0..k).
-ONE_DEVINL void topk_select(const float* score, int n, int k, int* out) {
-  TopkQ q;
-  for (int j = 0; j < n; ++j) { q.v[j] = score[j]; q.i[j] = j; }
+template <class Q>
+ONE_DEVINL void topk_run(Q& q, int n, int k, int* out) {
   if (k <= 0) return;
   if (k * 64 <= n) {
     tk_heap_select(q, 0, k, n);
@@ -137,7 +175,24 @@ ONE_DEVINL void topk_select(const float* score, int n, int k, int* out) {
     }
     if (!done) tk_insertion_sort(q, first, last);
   }
-  for (int j = 0; j < k; ++j) out[j] = q.i[j];
+  for (int j = 0; j < k; ++j) out[j] = q.gi(j);
+}
+
+// Select k of n scores; writes the chosen indices, in the reference's order, to out[0..k).
+ONE_DEVINL void topk_select(const float* score, int n, int k, int* out) {
+  if (false) {  // the register queue is slower than the local-memory one (measured)
+    TopkRegQ<8> q;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      q.v[j] = j < n ? score[j] : 0.f;
+      q.i[j] = j;
+    }
+    topk_run(q, n, k, out);
+  } else {
+    TopkMemQ q;
+    for (int j = 0; j < n; ++j) q.set(j, score[j], j);
+    topk_run(q, n, k, out);
+  }
 }
 
 }  // namespace one

@@ -222,6 +222,15 @@ class OneEngine:
         C.LIB.one_engine_error(self.h, ctypes.byref(code), ctypes.byref(where))
         return code.value, where.value
 
+    def profile_step(self, reps: int = 20, batch: Optional[int] = None):
+        """Mean microseconds of each launch of one decode step (CUDA events, warm caches)."""
+        n = 256
+        buf = (ctypes.c_float * n)()
+        m = C.LIB.one_engine_profile_step(self.h, batch or self.batch, reps, buf, n, self._stream())
+        if m < 0:
+            raise C.OneError("one_engine_profile_step failed: " + C.LIB.one_last_error().decode())
+        return [float(buf[i]) for i in range(m)]
+
     def step_launches(self, batch: Optional[int] = None) -> int:
         return int(C.LIB.one_engine_step_launches(self.h, batch or self.batch))
 
