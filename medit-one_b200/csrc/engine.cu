@@ -295,7 +295,7 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<64>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<128>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::kSmem));
-  const int attn_max = 200 * 1024;
+  const int attn_max = 220 * 1024;
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(row_attn_kernel<float, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
@@ -675,13 +675,13 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       Launch a;
       a.kind = L_ROW_ATTN;
       a.dtype = dt;
-      a.block = 32 * std::max(4, std::min(H, kAttnMaxThreads / 32));
-      a.grid = std::min(T, num_sms() * 4);
+      a.block = kAttnThreads;
+      a.grid = std::min((T + kAttnTok - 1) / kAttnTok, num_sms() * 2);
       a.nv = H <= 16 ? 16 : 64;
-      a.smem = attn_layout(H, Dh, c.r, c.num_experts, D, a.block, moe ? 1 : 0, es).total;
-      if (a.smem > 200 * 1024) return fail(ONE_ERR_UNSUPPORTED, "attention/router weights exceed shared memory (%zu B)", a.smem);
-      if (moe && (HH % 8 || D % 8 || (c.r * HH) % 8 || D > 8 * 256))
-        return fail(ONE_ERR_UNSUPPORTED, "router shapes: H*H and D must be multiples of 8, D <= 2048");
+      a.smem = attn_layout(H, Dh, c.r, c.num_experts, D, moe ? 1 : 0, es).total;
+      if (a.smem > 220 * 1024) return fail(ONE_ERR_UNSUPPORTED, "attention/router weights exceed shared memory (%zu B)", a.smem);
+      if (moe && (HH % 8 || D % 8 || (c.r * HH) % 8 || Dh % 8))
+        return fail(ONE_ERR_UNSUPPORTED, "router shapes: H*H, D and head_dim must be multiples of 8");
       RowAttnParams& q = a.ra;
       memset(&q, 0, sizeof(q));
       q.T = T; q.H = H; q.Dh = Dh; q.r = c.r; q.E = c.num_experts; q.k = c.top_k; q.use_moe = moe ? 1 : 0;

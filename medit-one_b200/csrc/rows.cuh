@@ -441,87 +441,154 @@ __device__ void cta_router(int r, int E, int k, const MoeRouter& R, int t, const
 }
 
 // Shared-memory layout of row_attn_kernel (byte offsets), shared by host and device.
+constexpr int kAttnTok = 2;            // tokens per CTA iteration
+constexpr int kAttnThreads = 384;      // 12 warps: per token 1 (hx_moe) + 1 (x_moe) + 4 (cx_moe)
+constexpr int kAttnCxWarps = 4;
+struct AttnTokLayout {
+  int row, cs, rot, qkv, o, xs, cxs, gl, gq, cv, part, scr, sc, sel, bytes;
+};
 struct AttnLayout {
-  int wqkv, bqkv, gate, gate_ld, experts, b2, row, cs, rot, qkv, o, xs, cxs, gl, gpart, cv, cpart, red, sc, sel, total;
+  int wqkv, bqkv, gate, gate_ld, experts, b2, tok0, total;
+  AttnTokLayout tk;
 };
 __host__ __device__ inline int attn_take(int& off, int bytes) {
   const int o = off;
   off = (off + bytes + 15) & ~15;
   return o;
 }
-__host__ __device__ inline AttnLayout attn_layout(int H, int Dh, int r, int E, int D, int nthreads, int use_moe, int es) {
+__host__ __device__ inline AttnLayout attn_layout(int H, int Dh, int r, int E, int D, int use_moe, int es) {
   AttnLayout L;
   int off = 0;
-  const int HD = H * Dh, HH = H * H, nw = nthreads / 32;
-  L.wqkv = attn_take(off, 3 * H * (Dh + 1) * 4);
+  const int HD = H * Dh, HH = H * H, Dp = Dh + 4;
+  L.wqkv = attn_take(off, 3 * H * Dp * 4);
   L.bqkv = attn_take(off, 3 * H * 4);
   L.gate_ld = HH + (es == 2 ? 2 : 1);  // odd row stride in 32-bit words: conflict-free rows
   L.gate = attn_take(off, use_moe ? 2 * r * L.gate_ld * es : 0);
   L.experts = attn_take(off, use_moe ? 3 * E * 4 : 0);
   L.b2 = attn_take(off, use_moe ? E * (2 * HH + D) * es : 0);
-  L.row = attn_take(off, 3 * HD * 4);
-  L.cs = attn_take(off, 2 * Dh * 4);
-  L.rot = attn_take(off, H * 2 * Dh * 4);
-  L.qkv = attn_take(off, H * 3 * H * 4);
-  L.o = attn_take(off, HH * 4);
-  L.xs = attn_take(off, HH * 4);
-  L.cxs = attn_take(off, use_moe ? D * 4 : 0);
-  L.gl = attn_take(off, 3 * r * 4);
-  L.gpart = attn_take(off, 4 * 2 * r * 4);
-  L.cv = attn_take(off, 3 * E * 4);
-  L.cpart = attn_take(off, 3 * 32 * 8);
-  L.red = attn_take(off, 3 * kMaxExperts * 8 * 8);  // [router][expert][chunk] partial sums
-  L.sc = attn_take(off, 3 * E * 4);
-  L.sel = attn_take(off, 3 * E * 4);
-  L.total = off;
+  L.tok0 = off;
+  int t = 0;
+  AttnTokLayout& k = L.tk;
+  k.row = attn_take(t, 3 * HD * 4);
+  k.cs = attn_take(t, 2 * Dh * 4);
+  k.rot = attn_take(t, H * 2 * Dp * 4);
+  k.qkv = attn_take(t, H * 3 * H * 4);
+  k.o = attn_take(t, HH * 4);
+  k.xs = attn_take(t, HH * 4);
+  k.cxs = attn_take(t, use_moe ? D * 4 : 0);
+  k.gl = attn_take(t, 3 * r * 4);
+  k.gq = attn_take(t, kAttnCxWarps * r * 4);          // per cx warp copy of the gate logits
+  k.cv = attn_take(t, (2 + kAttnCxWarps) * E * 4);
+  k.part = attn_take(t, kAttnCxWarps * kMaxExperts * 8);  // cx expert partial sums
+  k.scr = attn_take(t, 6 * 32 * 8);                   // per router warp scratch
+  k.sc = attn_take(t, 3 * E * 4);
+  k.sel = attn_take(t, 3 * E * 4);
+  k.bytes = t;
+  L.total = off + kAttnTok * t;
   return L;
 }
 
-// Feature attention (one/modeling_one.py:390-556) and the three LinearMoE routers for
-// one token per CTA iteration. Every weight the kernel reads (lin_q/k/v, the hx_moe /
-// x_moe gates, experts, bias2) is copied to shared memory before the dependency wait.
-//   phase A : warp per head: RoPE (rotate_half) on single_x * scale and on key into
-//             shared rows, then lane u computes projection output u of q|k|v (Dh -> H,
-//             bias, rounded), then softmax(q*k - max) in fp32 over lanes j < H, o = w*v.
-//   phase B : gate logits of hx_moe / x_moe (all threads, split dot products), softmax
-//             over r and expert factors 1 + silu(mean_r(g * e)) (a warp per router), the
-//             per-expert biased sums of all three routers in one pass (exact fp64, rounded
-//             once), the top-k restatement (a thread per router) and the combine.
-constexpr int kAttnMaxThreads = 384;
+ONE_DEVINL void named_bar(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 
+// softmax over the r gate logits in g[] (fp32, cast to the dtype), then the expert
+// factors c_e = 1 + silu(clamp(mean_r(rnd(g * e)))) (one/linear_moe.py:56-68) into c[].
+// One warp; `cp` is 32 doubles of scratch.
+template <typename T>
+ONE_DEVINL void warp_gate_factors(float* g, int r, const float* ex, int E, float* c, double* cp) {
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+  for (int j = lane; j < r; j += 32) mx = fmaxf(mx, g[j]);
+  mx = warp_max(mx);
+  float sum = 0.f;
+  for (int j = lane; j < r; j += 32) sum += expf(g[j] - mx);
+  sum = warp_sum(sum);
+  const float inv = 1.0f / sum;
+  __syncwarp();
+  for (int j = lane; j < r; j += 32) g[j] = rnd<T>(expf(g[j] - mx) * inv);
+  __syncwarp();
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int ne = min(32, E - e0);
+    const int slices = 32 / ne;
+    const int e = lane % ne, sl = lane / ne;
+    double acc = 0.0;
+    if (sl < slices)
+      for (int j = sl; j < r; j += slices) acc += (double)rnd<T>(g[j] * ex[e0 + e]);
+    cp[lane] = acc;
+    __syncwarp();
+    if (lane < ne) {
+      double s2 = 0.0;
+      for (int q = 0; q < slices; ++q) s2 += cp[q * ne + lane];
+      const float scv = fminf(fmaxf(rnd<T>((float)s2 / (float)r), -10.f), 10.f);
+      c[e0 + lane] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
+    }
+    __syncwarp();
+  }
+}
+
+// Per-expert partial sums over x[i0..i1) of rnd(rnd(x * c_e) + bias2[e, i]) for experts
+// e0..e0+7, reduced over the warp (exact fp64). Result valid in every lane.
+template <typename T>
+ONE_DEVINL void warp_expert_sums(const float* x, int i0, int i1, const T* B2, int in, const float* c, int e0, int E,
+                                 double (&acc)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.0;
+  for (int i = i0 + lane; i < i1; i += 32) {
+    const float xi = x[i];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (e0 + e < E) {
+        const float ce = c[e0 + e];
+        const float xc = ce == 1.0f ? xi : rnd<T>(xi * ce);
+        acc[e] += (double)rnd<T>(xc + ld<T>(B2 + (size_t)(e0 + e) * in + i));
+      }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
+}
+
+// mean of the selected biased inputs over x[i0..i1) (one/linear_moe.py:87-90)
+template <typename T>
+ONE_DEVINL void warp_combine(const float* x, int i0, int i1, const T* B2, int in, const float* c, const int* sel, int kk,
+                             T* out) {
+  const int lane = threadIdx.x & 31;
+  for (int i = i0 + lane; i < i1; i += 32) {
+    float s2 = 0.f;
+    for (int j = 0; j < kk; ++j) {
+      const int e = sel[j];
+      s2 += rnd<T>(rnd<T>(x[i] * c[e]) + ld<T>(B2 + (size_t)e * in + i));
+    }
+    st<T>(out + i, s2 / (float)kk);
+  }
+}
+
+// Feature attention (one/modeling_one.py:390-556) and the three LinearMoE routers,
+// kAttnTok tokens per CTA iteration. Every weight the kernel reads (lin_q/k/v, the
+// hx_moe / x_moe gates, experts, bias2) is copied to shared memory before the
+// dependency wait.
+//   phase A: warp per (token, head): RoPE (rotate_half) on single_x * scale and on key,
+//            lane u computes projection output u of q|k|v (Dh -> H, bias, rounded),
+//            softmax(q*k - max) in fp32 over lanes j < H, o = w * v.
+//   phase B: per token, warp 0 routes hx_moe, warp 1 x_moe (gate GEMV, softmax, expert
+//            factors, expert sums, top-k, combine) and warps 2..5 route cx_moe, each
+//            summing and combining a quarter of the 768 inputs; no CTA-wide barrier.
 template <typename T, int HMAX>
-__global__ void __launch_bounds__(kAttnMaxThreads, 2) row_attn_kernel(const RowAttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttnParams p) {
   extern __shared__ __align__(16) uint8_t smb[];
   const int H = p.H, Dh = p.Dh, HD = H * Dh, HH = H * H, r = p.r, E = p.E;
   const int D = p.use_moe ? p.rt[2].in : 0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nw = nthr >> 5;
-  const AttnLayout L = attn_layout(H, Dh, r, E, D, nthr, p.use_moe, (int)sizeof(T));
+  const AttnLayout L = attn_layout(H, Dh, r, E, D, p.use_moe, (int)sizeof(T));
   float* wqkv = reinterpret_cast<float*>(smb + L.wqkv);
   float* bqkv = reinterpret_cast<float*>(smb + L.bqkv);
   T* gate = reinterpret_cast<T*>(smb + L.gate);
   float* exps = reinterpret_cast<float*>(smb + L.experts);
   T* b2s = reinterpret_cast<T*>(smb + L.b2);
-  float* row = reinterpret_cast<float*>(smb + L.row);
-  float* cs = reinterpret_cast<float*>(smb + L.cs);
-  float* rot = reinterpret_cast<float*>(smb + L.rot);
-  float* qkv = reinterpret_cast<float*>(smb + L.qkv);
-  float* o = reinterpret_cast<float*>(smb + L.o);
-  float* xs = reinterpret_cast<float*>(smb + L.xs);
-  float* cxs = reinterpret_cast<float*>(smb + L.cxs);
-  float* gl = reinterpret_cast<float*>(smb + L.gl);
-  float* gpart = reinterpret_cast<float*>(smb + L.gpart);
-  float* cv = reinterpret_cast<float*>(smb + L.cv);
-  double* cpart = reinterpret_cast<double*>(smb + L.cpart);
-  double* red = reinterpret_cast<double*>(smb + L.red);
-  float* sc = reinterpret_cast<float*>(smb + L.sc);
-  int* sel = reinterpret_cast<int*>(smb + L.sel);
-  const int half = Dh / 2, Dp = Dh + 1;
+  const int half = Dh / 2, Dp = Dh + 4;
   const int inr[3] = {HH, HH, D};
   const int b2off[3] = {0, E * HH, 2 * E * HH};
 
-  // ---- weights to shared memory (not written by the previous kernel: before the wait),
-  // copied as 16-byte vectors
-  constexpr int VE = 16 / (int)sizeof(T);  // elements per 16-byte vector
+  // ---- weights to shared memory (not written by the previous kernel: before the wait)
   for (int v = tid; v < 3 * HD / 8; v += nthr) {
     const int u = (v * 8) / Dh, d0 = (v * 8) % Dh, which = u / H;
     const T* W = reinterpret_cast<const T*>(which == 0 ? p.wq : which == 1 ? p.wk : p.wv);
@@ -536,15 +603,12 @@ __global__ void __launch_bounds__(kAttnMaxThreads, 2) row_attn_kernel(const RowA
     bqkv[i] = ld<T>(Bb + j);
   }
   if (p.use_moe) {
-    {
-      // 32-bit copies into rows of gate_ld elements (an odd number of words)
-      const int wpr = HH * (int)sizeof(T) / 4, wld = L.gate_ld * (int)sizeof(T) / 4;
-      for (int w = tid; w < 2 * r * wpr; w += nthr) {
-        const int j = w / wpr, c = w % wpr, ri = j / r;
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.rt[ri].gate_w);
-        reinterpret_cast<uint32_t*>(gate)[j * wld + c] = src[(j % r) * wpr + c];
-      }
+    const int wpr = HH * (int)sizeof(T) / 4, wld = L.gate_ld * (int)sizeof(T) / 4;
+    for (int w = tid; w < 2 * r * wpr; w += nthr) {
+      const int j = w / wpr, c = w % wpr, ri = j / r;
+      reinterpret_cast<uint32_t*>(gate)[j * wld + c] = reinterpret_cast<const uint32_t*>(p.rt[ri].gate_w)[(j % r) * wpr + c];
     }
+    constexpr int VE = 16 / (int)sizeof(T);
     for (int ri = 0; ri < 3; ++ri) {
       const uint4* src = reinterpret_cast<const uint4*>(p.rt[ri].bias2);
       uint4* dst = reinterpret_cast<uint4*>(b2s + b2off[ri]);
@@ -556,45 +620,60 @@ __global__ void __launch_bounds__(kAttnMaxThreads, 2) row_attn_kernel(const RowA
   if (tid == 0) pdl_launch_dependents();
   pdl_wait();
 
-  for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
-    const int pos = p.counters[0] + (p.seq_len > 0 ? t % p.seq_len : 0);
-    // cos / sin (OneRotaryEmbedding, :159-182): fp32 inv_freq * pos, cast to the dtype
-    for (int i = tid; i < half; i += nthr) {
-      const float f = p.inv_freq[i] * (float)pos;
-      const float c = rnd<T>(cosf(f)), sn = rnd<T>(sinf(f));
-      cs[i] = c; cs[i + half] = c;
-      cs[Dh + i] = sn; cs[Dh + i + half] = sn;
-    }
-    const T* pr = reinterpret_cast<const T*>(p.proj) + (size_t)t * 3 * HD;
-    for (int i = tid * 8; i < 3 * HD; i += nthr * 8) {
-      float v[8];
-      load8(pr + i, v);
-      if (i < HD)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = rnd<T>(v[e] * p.attn_scale);  // :405
-#pragma unroll
-      for (int e = 0; e < 8; ++e) row[i + e] = v[e];
-    }
-    if (p.use_moe) {
-      const T* X = reinterpret_cast<const T*>(p.rt[2].x) + (size_t)t * p.rt[2].ldx;
-      for (int i = tid * 8; i < D; i += nthr * 8) {
-        float v[8];
-        load8(X + i, v);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) cxs[i + e] = v[e];
+  for (int t0 = blockIdx.x * kAttnTok; t0 < p.T; t0 += gridDim.x * kAttnTok) {
+    const int ntok = min(kAttnTok, p.T - t0);
+    // ---- phase 0: rows of each token
+    for (int k = 0; k < ntok; ++k) {
+      uint8_t* tb = smb + L.tok0 + k * L.tk.bytes;
+      float* row = reinterpret_cast<float*>(tb + L.tk.row);
+      float* cs = reinterpret_cast<float*>(tb + L.tk.cs);
+      const int t = t0 + k;
+      const int pos = p.counters[0] + (p.seq_len > 0 ? t % p.seq_len : 0);
+      // cos / sin (OneRotaryEmbedding, :159-182): fp32 inv_freq * pos, cast to the dtype
+      for (int i = tid; i < half; i += nthr) {
+        const float f = p.inv_freq[i] * (float)pos;
+        const float c = rnd<T>(cosf(f)), sn = rnd<T>(sinf(f));
+        cs[i] = c; cs[i + half] = c;
+        cs[Dh + i] = sn; cs[Dh + i + half] = sn;
       }
-      const T* G = reinterpret_cast<const T*>(p.rt[2].glog) + (size_t)t * r;
-      for (int j = tid; j < r; j += nthr) gl[2 * r + j] = ld<T>(G + j);
+      const T* pr = reinterpret_cast<const T*>(p.proj) + (size_t)t * 3 * HD;
+      for (int i = tid * 8; i < 3 * HD; i += nthr * 8) {
+        float v[8];
+        load8(pr + i, v);
+        if (i < HD)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = rnd<T>(v[e] * p.attn_scale);  // :405
+#pragma unroll
+        for (int e = 0; e < 8; ++e) row[i + e] = v[e];
+      }
+      if (p.use_moe) {
+        float* cxs = reinterpret_cast<float*>(tb + L.tk.cxs);
+        float* gl = reinterpret_cast<float*>(tb + L.tk.gl);
+        const T* X = reinterpret_cast<const T*>(p.rt[2].x) + (size_t)t * p.rt[2].ldx;
+        for (int i = tid * 8; i < D; i += nthr * 8) {
+          float v[8];
+          load8(X + i, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) cxs[i + e] = v[e];
+        }
+        const T* G = reinterpret_cast<const T*>(p.rt[2].glog) + (size_t)t * r;
+        for (int j = tid; j < r; j += nthr) gl[2 * r + j] = ld<T>(G + j);
+      }
     }
     __syncthreads();
 
-    // ---- phase A: one warp per head
-    for (int h = warp; h < H; h += nw) {
+    // ---- phase A: one warp per (token, head)
+    for (int pr_ = warp; pr_ < ntok * H; pr_ += nw) {
+      const int k = pr_ / H, h = pr_ % H;
+      uint8_t* tb = smb + L.tok0 + k * L.tk.bytes;
+      const float* row = reinterpret_cast<const float*>(tb + L.tk.row);
+      const float* cs = reinterpret_cast<const float*>(tb + L.tk.cs);
+      float* xr = reinterpret_cast<float*>(tb + L.tk.rot) + h * 2 * Dp;
+      float* kr = xr + Dp;
+      float* qh = reinterpret_cast<float*>(tb + L.tk.qkv) + h * 3 * H;
       const float* sx = row + h * Dh;
       const float* sk = row + HD + h * Dh;
       const float* sv = row + 2 * HD + h * Dh;
-      float* xr = rot + h * 2 * Dh;
-      float* kr = xr + Dh;
       for (int d = lane; d < Dh; d += 32) {
         const float px = d < half ? -sx[d + half] : sx[d - half];
         const float pk = d < half ? -sk[d + half] : sk[d - half];
@@ -602,13 +681,20 @@ __global__ void __launch_bounds__(kAttnMaxThreads, 2) row_attn_kernel(const RowA
         kr[d] = rnd<T>(rnd<T>(sk[d] * cs[d]) + rnd<T>(pk * cs[Dh + d]));
       }
       __syncwarp();
-      float* qh = qkv + h * 3 * H;
       for (int u = lane; u < 3 * H; u += 32) {
         const int which = u / H;
         const float* src = which == 0 ? xr : which == 1 ? kr : sv;
         const float* w = wqkv + u * Dp;
         float acc = 0.f;
-        for (int d = 0; d < Dh; ++d) acc = fmaf(w[d], src[d], acc);
+        if (which < 2) {
+          for (int d = 0; d < Dh; d += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(w + d);
+            const float4 b = *reinterpret_cast<const float4*>(src + d);
+            acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc); acc = fmaf(a.z, b.z, acc); acc = fmaf(a.w, b.w, acc);
+          }
+        } else {
+          for (int d = 0; d < Dh; ++d) acc = fmaf(w[d], src[d], acc);
+        }
         qh[u] = rnd<T>(acc + bqkv[u]);
       }
       __syncwarp();
@@ -626,135 +712,106 @@ __global__ void __launch_bounds__(kAttnMaxThreads, 2) row_attn_kernel(const RowA
         float w = ex * (1.0f / sum);
         w = isnan(w) ? 1.0f / (float)H : rnd<T>(w);
         const float ov = rnd<T>(w * v);
-        o[h * H + lane] = ov;
-        xs[h * H + lane] = fminf(fmaxf(ov, -1e4f), 1e4f);  // LinearMoE input clamp (:53)
+        reinterpret_cast<float*>(tb + L.tk.o)[h * H + lane] = ov;
+        reinterpret_cast<float*>(tb + L.tk.xs)[h * H + lane] = fminf(fmaxf(ov, -1e4f), 1e4f);  // LinearMoE clamp (:53)
       }
     }
     __syncthreads();
     if (p.o) {
-      T* O = reinterpret_cast<T*>(p.o) + (size_t)t * HH;
-      for (int i = tid; i < HH; i += nthr) st<T>(O + i, o[i]);
-    }
-    if (!p.use_moe) {
-      __syncthreads();
-      continue;
-    }
-    // ---- phase B1: gate logits of hx_moe / x_moe (:56) on clamp(o) (:53): a thread per
-    // (gate row, slice of the row), partial sums added in slice order
-    {
-      const int n2 = 2 * r;
-      const int parts = max(1, min(nthr / n2, 4));
-      const int chunk = (HH + parts - 1) / parts;
-      for (int w = tid; w < n2 * parts; w += nthr) {
-        const int j = w % n2, part = w / n2;
-        const T* Wg = gate + j * L.gate_ld;
-        const int i0 = part * chunk, i1 = min(HH, i0 + chunk);
-        float acc = 0.f;
-        for (int i = i0; i < i1; ++i) acc = fmaf(ld<T>(Wg + i), xs[i], acc);
-        gpart[part * n2 + j] = acc;
-      }
-      __syncthreads();
-      for (int j = tid; j < n2; j += nthr) {
-        float acc = 0.f;
-        for (int part = 0; part < parts; ++part) acc += gpart[part * n2 + j];
-        gl[j] = rnd<T>(acc);
+      for (int k = 0; k < ntok; ++k) {
+        const float* o = reinterpret_cast<const float*>(smb + L.tok0 + k * L.tk.bytes + L.tk.o);
+        T* O = reinterpret_cast<T*>(p.o) + (size_t)(t0 + k) * HH;
+        for (int i = tid; i < HH; i += nthr) st<T>(O + i, o[i]);
       }
     }
-    __syncthreads();
-    // ---- phase B2: softmax over r and the expert factors, one warp per router
-    if (warp < 3) {
-      float* g = gl + warp * r;
-      float mx = -INFINITY;
-      for (int j = lane; j < r; j += 32) mx = fmaxf(mx, g[j]);
-      mx = warp_max(mx);
-      float sum = 0.f;
-      for (int j = lane; j < r; j += 32) sum += expf(g[j] - mx);
-      sum = warp_sum(sum);
-      const float inv = 1.0f / sum;
-      __syncwarp();
-      for (int j = lane; j < r; j += 32) g[j] = rnd<T>(expf(g[j] - mx) * inv);
-      __syncwarp();
-      // mean over r of rnd(g * e): lanes split as (expert e, slice); exact fp64 partial sums
-      const float* ex = exps + warp * E;
-      double* cp = cpart + warp * 32;
-      for (int e0 = 0; e0 < E; e0 += 32) {
-        const int ne = min(32, E - e0);
-        const int slices = 32 / ne;
-        const int e = lane % ne, sl = lane / ne;
-        double acc = 0.0;
-        if (sl < slices)
-          for (int j = sl; j < r; j += slices) acc += (double)rnd<T>(g[j] * ex[e0 + e]);
-        cp[lane] = acc;
-        __syncwarp();
-        if (lane < ne) {
-          double s2 = 0.0;
-          for (int q = 0; q < slices; ++q) s2 += cp[q * ne + lane];
-          const float scv = fminf(fmaxf(rnd<T>((float)s2 / (float)r), -10.f), 10.f);
-          cv[warp * E + e0 + lane] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
-        }
-        __syncwarp();
-      }
-    }
-    __syncthreads();
-    // ---- phase B3: per-expert sums of x * c_e + bias2[e] (:71-80) for the three routers:
-    // a warp per (router, expert, 256-element chunk), exact fp64 sums, rounded once
-    {
-      constexpr int CH = 256;
-      const int nch[3] = {(HH + CH - 1) / CH, (HH + CH - 1) / CH, (D + CH - 1) / CH};
-      const int items = E * (nch[0] + nch[1] + nch[2]);
-      for (int it = warp; it < items; it += nw) {
-        int ri = 0, rem = it;
-        while (rem >= E * nch[ri]) { rem -= E * nch[ri]; ++ri; }
-        const int e = rem / nch[ri], ch = rem % nch[ri];
-        const int in = inr[ri];
-        const float* x = ri < 2 ? xs : cxs;
-        const T* B2 = b2s + b2off[ri] + (size_t)e * in;
-        const float c = cv[ri * E + e];
-        double acc = 0.0;
-        const int i1 = min(in, (ch + 1) * CH);
-        if (c == 1.0f) {
-          for (int i = ch * CH + lane; i < i1; i += 32) acc += (double)rnd<T>(x[i] + ld<T>(B2 + i));
+    if (p.use_moe) {
+      // ---- phase B: routers, warps grouped per token slot (6 warps each)
+      const int k = warp / 6, role = warp % 6;
+      if (k < ntok && warp < 6 * kAttnTok) {
+        const int t = t0 + k;
+        uint8_t* tb = smb + L.tok0 + k * L.tk.bytes;
+        const float* xs = reinterpret_cast<const float*>(tb + L.tk.xs);
+        const float* cxs = reinterpret_cast<const float*>(tb + L.tk.cxs);
+        float* gl = reinterpret_cast<float*>(tb + L.tk.gl);
+        float* cvb = reinterpret_cast<float*>(tb + L.tk.cv);
+        double* part = reinterpret_cast<double*>(tb + L.tk.part);
+        float* sc = reinterpret_cast<float*>(tb + L.tk.sc);
+        int* sel = reinterpret_cast<int*>(tb + L.tk.sel);
+        const int kk = min(p.k, E);
+        if (role < 2) {
+          // hx_moe (role 0) / x_moe (role 1) on clamp(o)
+          const int ri = role;
+          float* g = gl + ri * r;
+          const T* Wg = gate + (size_t)ri * r * L.gate_ld;
+          for (int j = lane; j < r; j += 32) {
+            const T* wr = Wg + j * L.gate_ld;
+            float acc = 0.f;
+            for (int i = 0; i < HH; ++i) acc = fmaf(ld<T>(wr + i), xs[i], acc);
+            g[j] = rnd<T>(acc);  // gate logits (:56)
+          }
+          __syncwarp();
+          float* c = cvb + ri * E;
+          double* cp = reinterpret_cast<double*>(tb + L.tk.scr) + role * 32;
+          warp_gate_factors<T>(g, r, exps + ri * E, E, c, cp);
+          const T* B2 = b2s + b2off[ri];
+          for (int e0 = 0; e0 < E; e0 += 8) {
+            double acc[8];
+            warp_expert_sums<T>(xs, 0, HH, B2, HH, c, e0, E, acc);
+            if (lane == 0)
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                if (e0 + e < E) sc[ri * E + e0 + e] = rnd<T>(__double2float_rn(acc[e]));
+          }
+          __syncwarp();
+          if (lane == 0) {
+            int chosen[kMaxExperts];
+            topk_select(sc + ri * E, E, kk, chosen);
+            for (int j = 0; j < kk; ++j) {
+              sel[ri * E + j] = chosen[j];
+              if (p.rt[ri].idx_out) p.rt[ri].idx_out[(size_t)t * kk + j] = chosen[j];
+            }
+          }
+          __syncwarp();
+          warp_combine<T>(xs, 0, HH, B2, HH, c, sel + ri * E, kk, reinterpret_cast<T*>(p.rt[ri].comb) + (size_t)t * HH);
         } else {
-          for (int i = ch * CH + lane; i < i1; i += 32) acc += (double)rnd<T>(rnd<T>(x[i] * c) + ld<T>(B2 + i));
+          // cx_moe on clamp(cx): four warps, each a quarter of the inputs
+          const int q = role - 2;
+          const int bar = 1 + k;
+          float* g = gl + 2 * r;
+          float* c = cvb + (2 + q) * E;
+          // each warp normalises its own copy of the gate logits
+          float* gg = reinterpret_cast<float*>(tb + L.tk.gq) + q * r;
+          for (int j = lane; j < r; j += 32) gg[j] = g[j];
+          __syncwarp();
+          warp_gate_factors<T>(gg, r, exps + 2 * E, E, c, reinterpret_cast<double*>(tb + L.tk.scr) + role * 32);
+          const int qlen = (D + kAttnCxWarps - 1) / kAttnCxWarps;
+          const int i0 = q * qlen, i1 = min(D, i0 + qlen);
+          const T* B2 = b2s + b2off[2];
+          for (int e0 = 0; e0 < E; e0 += 8) {
+            double acc[8];
+            warp_expert_sums<T>(cxs, i0, i1, B2, D, c, e0, E, acc);
+            if (lane == 0)
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                if (e0 + e < E) part[q * kMaxExperts + e0 + e] = acc[e];
+          }
+          named_bar(bar, 32 * kAttnCxWarps);
+          if (q == 0 && lane == 0) {
+            for (int e = 0; e < E; ++e) {
+              double s2 = 0.0;
+              for (int qq = 0; qq < kAttnCxWarps; ++qq) s2 += part[qq * kMaxExperts + e];
+              sc[2 * E + e] = rnd<T>(__double2float_rn(s2));
+            }
+            int chosen[kMaxExperts];
+            topk_select(sc + 2 * E, E, kk, chosen);
+            for (int j = 0; j < kk; ++j) {
+              sel[2 * E + j] = chosen[j];
+              if (p.rt[2].idx_out) p.rt[2].idx_out[(size_t)t * kk + j] = chosen[j];
+            }
+          }
+          named_bar(bar, 32 * kAttnCxWarps);
+          warp_combine<T>(cxs, i0, i1, B2, D, c, sel + 2 * E, kk, reinterpret_cast<T*>(p.rt[2].comb) + (size_t)t * D);
         }
-        acc = warp_sum_d(acc);
-        if (lane == 0) red[(ri * kMaxExperts + e) * 8 + ch] = acc;
-      }
-      __syncthreads();
-      for (int q = tid; q < 3 * E; q += nthr) {
-        const int ri = q / E, e = q % E;
-        double s2 = 0.0;
-        for (int ch = 0; ch < nch[ri]; ++ch) s2 += red[(ri * kMaxExperts + e) * 8 + ch];
-        sc[ri * E + e] = rnd<T>(__double2float_rn(s2));
-      }
-      __syncthreads();
-    }
-    // ---- phase B4: top-k (:83-84), a thread per router
-    const int kk = min(p.k, E);
-    if (lane == 0 && warp < 3) {
-      int chosen[kMaxExperts];
-      topk_select(sc + warp * E, E, kk, chosen);
-      for (int j = 0; j < kk; ++j) {
-        sel[warp * E + j] = chosen[j];
-        if (p.rt[warp].idx_out) p.rt[warp].idx_out[(size_t)t * kk + j] = chosen[j];
-      }
-    }
-    __syncthreads();
-    // ---- phase B5: combine, the mean of the selected biased inputs (:87-90)
-    {
-      const int ntot = 2 * HH + D;
-      for (int g = tid; g < ntot; g += nthr) {
-        const int ri = g < HH ? 0 : (g < 2 * HH ? 1 : 2);
-        const int i = ri == 0 ? g : (ri == 1 ? g - HH : g - 2 * HH);
-        const float xi = ri < 2 ? xs[i] : cxs[i];
-        const T* B2 = b2s + b2off[ri];
-        const float* c = cv + ri * E;
-        float s2 = 0.f;
-        for (int j = 0; j < kk; ++j) {
-          const int e = sel[ri * E + j];
-          s2 += rnd<T>(rnd<T>(xi * c[e]) + ld<T>(B2 + (size_t)e * inr[ri] + i));
-        }
-        st<T>(reinterpret_cast<T*>(p.rt[ri].comb) + (size_t)t * inr[ri] + i, s2 / (float)kk);
       }
     }
     __syncthreads();
