@@ -249,6 +249,10 @@ def run_native(args, ws, rank, local):
     if code != (0, 0):
         raise RuntimeError(f"device error {code}")
     value = ws * BATCH * steps / (ms_max / 1000.0)
+    # outside the timed region: every rank's generated tokens to every rank (NCCL all-gather)
+    from one import distributed as Dd
+    tokens = Dd.gather_tokens(eng.history(min(steps + warmup, eng.hist_cap), BATCH).t().contiguous(), BATCH * ws)
+    assert tokens.shape[0] == BATCH * ws
 
     # e2e through the public step API: pinned host ids in, next ids out, every step
     ids_host = torch.randint(0, cfg.vocab_size, (BATCH,), dtype=torch.int32, generator=g).pin_memory()

@@ -73,3 +73,99 @@ def test_linear_moe_all_ties_reference_order():
         x = torch.randn(5, 144).bfloat16().cuda()
         _, idx = native_linear_moe(x, p, 2)
         np.testing.assert_array_equal(idx.cpu().numpy(), g[f"alltie_e{E}_idx"])
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+def test_rotary_and_cumsum_match_reference(dt):
+    from one import turbo_ops
+    g = load("ops.npz")
+    from oracle import one_oracle as O
+    inv = O.rope_inv_freq(64, 10000.0).cuda()
+    x = torch.zeros(1, 300, 64, dtype=DT[dt], device="cuda")
+    c, s = turbo_ops.turbo_rotary_embedding(x, torch.arange(0, 300).unsqueeze(0).cuda(), inv)
+    assert_close(c.float().cpu().numpy(), g[f"rope_cos_{dt}"], dt, "cos")
+    assert_close(s.float().cpu().numpy(), g[f"rope_sin_{dt}"], dt, "sin")
+    xs = torch.from_numpy(g[f"cumsum_x_{dt}"]).to(DT[dt]).cuda()
+    y = turbo_ops.turbo_cumsum_and_normalize(xs, 50)
+    assert_close(y.float().cpu().numpy(), g[f"cumsum_y_{dt}"], dt, "cumsum_and_normalize")
+
+
+@pytest.mark.parametrize("n", [64, 96])
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_attention_matches_reference(n, dt, causal):
+    from one import turbo_ops
+    g = load("attention.npz")
+    q, k, v = (torch.from_numpy(g[f"{c}_n{n}"]).to(DT[dt]).cuda() for c in "qkv")
+    out = turbo_ops.turbo_flash_attention(q, k, v, causal=causal)
+    tag = f"n{n}_{dt}_{'c' if causal else 'nc'}"
+    assert_close(out.float().cpu().numpy(), g[f"turbo_{tag}"], dt, "attention")
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+def test_combined_rope_attention_matches_oracle(dt):
+    from one import turbo_ops
+    import one_turbo
+    from oracle import one_oracle as O
+    gen = torch.Generator().manual_seed(5)
+    H, Dh, B, T = 12, 64, 3, 4
+    sx, ky, va = (torch.randn(B, H, T, Dh, generator=gen).to(DT[dt]) for _ in range(3))
+    lins = [torch.nn.Linear(Dh, H).to(DT[dt]) for _ in range(3)]
+    with torch.no_grad():
+        for lin in lins:
+            lin.weight.copy_(torch.randn(H, Dh, generator=gen) * 0.1)
+            lin.bias.copy_(torch.randn(H, generator=gen) * 0.1)
+    cos, sin = O.rope_cos_sin(O.rope_inv_freq(Dh, 1e4), torch.arange(7, 7 + T).unsqueeze(0), DT[dt])
+    ref = O.feature_attention(sx, ky, va, cos, sin, *[(l.weight, l.bias) for l in lins])
+    got = turbo_ops.turbo_combined_rope_attention(sx.cuda(), ky.cuda(), va.cuda(), cos.cuda(), sin.cuda(),
+                                                  *[l.cuda() for l in lins], T)
+    assert_close(got.float().cpu().numpy(), ref.float().numpy(), dt, "combined rope attention")
+    # the legacy one_turbo signature: transposed weights, no biases
+    nob = [(l.weight, None) for l in lins]
+    ref2 = O.feature_attention(sx, ky, va, cos, sin, *nob)
+    got2 = one_turbo.combined_rope_attention(sx.cuda(), ky.cuda(), va.cuda(), cos.cuda(), sin.cuda(),
+                                             *[l.weight.t().cuda() for l in lins], T)
+    assert_close(got2.float().cpu().numpy(), ref2.float().numpy(), dt, "one_turbo.combined_rope_attention")
+
+
+def test_linear_moe_module_matches_reference():
+    from one.initialization import moe_params
+    from one.linear_moe import LinearMoE
+    g = load("linear_moe.npz")
+    tag, fin, fout, E, k, N, seed = CASES[0]
+    p = moe_params(fin, fout, E, 64, seed, torch.bfloat16)
+    m = LinearMoE(fin, fout, bias=True, num_experts=E, top_k=k, r=64).to(torch.bfloat16)
+    with torch.no_grad():
+        m.weight.copy_(p["weight"]); m.bias.copy_(p["bias"]); m.gate.weight.copy_(p["gate"])
+        m.experts.copy_(p["experts"]); m.bias2.copy_(p["bias2"])
+    m = m.cuda()
+    x = torch.randn(N, fin, generator=torch.Generator().manual_seed(seed + 100)).to(torch.bfloat16).cuda()
+    y = m(x)
+    np.testing.assert_array_equal(m.last_indices.cpu().numpy(), g[f"{tag}_bf16_idx"])
+    assert_close(y.float().cpu().numpy(), g[f"{tag}_bf16_y"], "bf16", "LinearMoE module")
+
+
+def test_causal_lm_api_matches_reference():
+    """OneForCausalLM (same parameter names as the reference) loads the seeded state dict and
+    reproduces the reference's logits, cached decode and greedy tokens."""
+    from one.configuration_one import tiny_config
+    from one.initialization import init_state_dict
+    from one.modeling_one import OneEngineCache, OneForCausalLM
+    g = load("forward_bf16.npz")
+    cfg = tiny_config()
+    model = OneForCausalLM(cfg)
+    sd = init_state_dict(cfg, 0, torch.float32)
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected and set(missing) <= {"lm_head.weight"}
+    model = model.to(torch.bfloat16).cuda()
+    out = model(input_ids=torch.from_numpy(g["ids"]).cuda())
+    assert_close(out.logits.float().cpu()[..., :512].numpy(), g["logits_slice"], "bf16", "forward logits")
+    d = load("decode_bf16.npz")
+    cache = OneEngineCache()
+    model(input_ids=torch.from_numpy(d["prompt"]).cuda(), past_key_values=cache, use_cache=True)
+    gen = torch.from_numpy(d["generated"]).cuda()
+    for s in range(gen.shape[1]):
+        out = model(input_ids=gen[:, s:s + 1], past_key_values=cache, use_cache=True)
+        assert_close(out.logits[:, 0].float().cpu()[:, :512].numpy(), d["logits_slice"][s], "bf16", f"decode {s}")
+    seq = model.generate_greedy(torch.from_numpy(d["prompt"]).cuda(), gen.shape[1])
+    assert (seq[:, 12:].cpu().numpy() == d["generated"]).mean() >= 0.9
