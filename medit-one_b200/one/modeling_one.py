@@ -163,18 +163,20 @@ class OneForCausalLM(OnePreTrainedModel, GenerationMixin):
 
     # ------------------------------------------------------------------ engine
     def engine(self, max_batch: int = 256, max_tokens: Optional[int] = None, max_positions: int = 8192):
-        """The OneEngine over this model's current parameters (built on first use)."""
+        """The OneEngine over this model's current parameters. Reused while its capacity
+        covers the request; otherwise rebuilt (which drops any decode state)."""
         from .engine import OneEngine
         p = self.model.embed_tokens.weight
         if not p.is_cuda:
             raise RuntimeError("OneForCausalLM runs on the B200 engine: move the model to CUDA")
-        key = (p.device, p.dtype, max_batch, max_tokens, max_positions)
-        if self._engine is None or self._engine_key != key:
+        max_tokens = max_tokens or max_batch
+        e = self._engine
+        if (e is None or e.device != p.device or e.dtype != p.dtype or e.max_batch < max_batch
+                or e.max_tokens < max_tokens or e.max_positions < max_positions):
             sd = {k: v for k, v in self.state_dict().items()}
             sd.setdefault("lm_head.weight", self.lm_head.weight)
             self._engine = OneEngine(self.config, sd, p.device, p.dtype, max_batch=max_batch,
-                                     max_tokens=max_tokens or max(max_batch, 4096), max_positions=max_positions)
-            self._engine_key = key
+                                     max_tokens=max(max_tokens, 4096), max_positions=max_positions)
         return self._engine
 
     def refresh_engine(self):
@@ -189,10 +191,15 @@ class OneForCausalLM(OnePreTrainedModel, GenerationMixin):
         if input_ids is None:
             raise ValueError("the engine takes input_ids")
         B, S = input_ids.shape
-        eng = self.engine(max_batch=max(B, 1), max_tokens=max(B * S, B))
         cache = past_key_values
         if use_cache and cache is None:
             cache = OneEngineCache()
+        if cache is None or cache.seen_tokens == 0:
+            eng = self.engine(max_batch=B, max_tokens=B * S)
+        else:
+            eng = self._engine
+            if eng is None or eng.batch != B:
+                raise RuntimeError("this cache's sequences are not the engine's current batch")
         if cache is None or cache.seen_tokens == 0:
             logits = eng.prefill(input_ids, logits="all")
             if cache is not None:

@@ -116,15 +116,20 @@ def test_combined_rope_attention_matches_oracle(dt):
             lin.weight.copy_(torch.randn(H, Dh, generator=gen) * 0.1)
             lin.bias.copy_(torch.randn(H, generator=gen) * 0.1)
     cos, sin = O.rope_cos_sin(O.rope_inv_freq(Dh, 1e4), torch.arange(7, 7 + T).unsqueeze(0), DT[dt])
-    ref = O.feature_attention(sx, ky, va, cos, sin, *[(l.weight, l.bias) for l in lins])
-    got = turbo_ops.turbo_combined_rope_attention(sx.cuda(), ky.cuda(), va.cuda(), cos.cuda(), sin.cuda(),
-                                                  *[l.cuda() for l in lins], T)
+    with torch.no_grad():
+        ref = O.feature_attention(sx, ky, va, cos, sin, *[(l.weight, l.bias) for l in lins])
+    import copy
+    with torch.no_grad():
+        got = turbo_ops.turbo_combined_rope_attention(sx.cuda(), ky.cuda(), va.cuda(), cos.cuda(), sin.cuda(),
+                                                      *[copy.deepcopy(l).cuda() for l in lins], T)
     assert_close(got.float().cpu().numpy(), ref.float().numpy(), dt, "combined rope attention")
     # the legacy one_turbo signature: transposed weights, no biases
-    nob = [(l.weight, None) for l in lins]
-    ref2 = O.feature_attention(sx, ky, va, cos, sin, *nob)
-    got2 = one_turbo.combined_rope_attention(sx.cuda(), ky.cuda(), va.cuda(), cos.cuda(), sin.cuda(),
-                                             *[l.weight.t().cuda() for l in lins], T)
+    nob = [(l.weight.detach(), None) for l in lins]
+    with torch.no_grad():
+        ref2 = O.feature_attention(sx, ky, va, cos, sin, *nob)
+    with torch.no_grad():
+        got2 = one_turbo.combined_rope_attention(sx.cuda(), ky.cuda(), va.cuda(), cos.cuda(), sin.cuda(),
+                                                 *[l.weight.t().cuda() for l in lins], T)
     assert_close(got2.float().cpu().numpy(), ref2.float().numpy(), dt, "one_turbo.combined_rope_attention")
 
 
