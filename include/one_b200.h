@@ -139,6 +139,21 @@ int one_linear_moe(const void* x, int32_t n, int32_t fin, int32_t fout, const vo
                    int32_t top_k, int32_t dtype, void* out, int32_t* idx_out, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* one_linear_moe without a workspace argument, for callers that cannot allocate device
+ * memory: a host program that binds this library through a foreign-function interface and only
+ * holds the device pointers it is handed, or a process whose device memory belongs entirely to
+ * another runtime's pool. No counterpart in the reference. The scratch is a static array in the
+ * library image of ONE_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library
+ * until the process exits; calls needing more (n * fin too large) fail with ONE_ERR_INVALID.
+ * The first call on a device looks the array's device address up (cudaGetSymbolAddress) with
+ * that device current, so make that first call before any stream capture. Every call shares the
+ * one array: calls whose work overlaps on the GPU (other streams, other host threads) race;
+ * serialise them. No call allocates or frees device memory. */
+#define ONE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+int one_linear_moe_noalloc(const void* x, int32_t n, int32_t fin, int32_t fout, const void* weight, const void* bias,
+                           const void* gate_w, const void* experts, const void* bias2, int32_t num_experts, int32_t r,
+                           int32_t top_k, int32_t dtype, void* out, int32_t* idx_out, void* stream);
+
 /* Replaces one_turbo.moe_routing (csrc/one_kernels.cpp:65-74): the LinearMoE router
  * only. comb [n, fin] = mean of the selected biased inputs, idx_out [n, top_k]. */
 int one_moe_routing(const void* x, int32_t n, int32_t fin, const void* gate_logits, const void* experts, const void* bias2,

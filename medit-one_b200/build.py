@@ -41,7 +41,7 @@ def build(force: bool = False, verbose: bool = True) -> str:
     dig = _digest()
     if not force and os.path.exists(OUT) and os.path.exists(stamp) and open(stamp).read().strip() == dig:
         return OUT
-    cmd = [NVCC, *FLAGS, "-o", OUT, os.path.join(CSRC, "engine.cu")]
+    cmd = [NVCC, *FLAGS, "-o", OUT, os.path.join(CSRC, "engine.cu"), os.path.join(CSRC, "linear_moe_noalloc.cu")]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

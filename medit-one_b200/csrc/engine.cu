@@ -51,6 +51,8 @@ static int fail(int code, const char* fmt, ...) {
   } while (0)
 
 extern "C" int one_abi_version(void) { return ONE_B200_ABI_VERSION; }
+// error reporting for the library's other translation units (not exported)
+extern "C" __attribute__((visibility("hidden"))) int one_set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 extern "C" const char* one_last_error(void) { return g_err.c_str(); }
 
 // ------------------------------------------------------------------ TMA descriptors

@@ -52,6 +52,8 @@ SIGNATURES = {
     "one_linear_moe_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "one_linear_moe": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "one_linear_moe_noalloc": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "one_moe_routing": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                 c_int32, c_void_p, c_void_p, c_void_p]),
     "one_rotary_embedding": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32, c_void_p, c_void_p,
