@@ -229,6 +229,9 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
 
 // ------------------------------------------------------------------ programmatic dependent launch
 // griddepcontrol is a no-op when the launch carries no programmatic dependency.
+ONE_DEVINL void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 ONE_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 ONE_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -182,7 +182,7 @@ static int pick_bn(int T, int m_tiles_total) {
   if (T >= 2048) return 128;
   for (int bn : {256, 128, 64}) {
     const int ctas = m_tiles_total * ((T + bn - 1) / bn);
-    if (bn <= T * 2 && ctas >= 2 * num_sms()) return bn;
+    if (bn <= T * 2 && ctas >= num_sms()) return bn;
   }
   return T > 32 ? 64 : 32;
 }
@@ -282,11 +282,15 @@ static cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
+  static const bool pdl = [] {
+    const char* v = getenv("ONE_B200_NO_PDL");
+    return !(v && v[0] == '1');
+  }();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -135,7 +135,7 @@ ONE_DEVINL void epi_gelu_pair(const GemmProblem& P, int n_even, int t, float g, 
 }
 
 
-// E2 of the tensor-core epilogue (and the whole epilogue of nothing else): S holds the
+// Whole-tile epilogue over a staged fp32 tile (kept for reference use by other kernels): S holds the
 // fp32 accumulator of rows n_base .. n_base+127 for tokens t_base .. t_base+tn-1, laid
 // out S[t_local * 128 + n_local]. Rows >= Nw are padding. Requires Nw % 8 == 0 (16 for
 // GELU_UP), 8-aligned leading dimensions and 16-byte-aligned pointers (checked by the
@@ -267,8 +267,182 @@ struct TcCfg {
   static constexpr int kThreads = 192;  // w0 TMA, w1 MMA + TMEM owner, w2..5 epilogue
 };
 
+// Epilogue of the tensor-core GEMM, run by the 128 threads of warps 2..5 (e = thread - 64).
+//   prefetch: right after the dependency wait, each thread loads the bias of its 8-row slice
+//             and, for the kinds that read an activation (hx, mean), the aux vectors of its
+//             output units into registers, so no global load sits behind the accumulator.
+//   E1: the TMEM lane quarter (warp % 4) is copied into a shared fp32 tile S[token][row]
+//       (the drained pipeline buffers), kChunk tokens at a time.
+//   E2: unit = (token, 8 consecutive rows) [GELU_UP: (token, 8 outputs from 16 rows)];
+//       thread e owns the row slice e % 16 (e % 8) of every 8th (16th) token; 16-byte stores.
 template <int BN>
-__global__ void __launch_bounds__(192, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
+__device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProblem& P, float* S, uint32_t tmem,
+                                            uint64_t* accb, int m_tile, int n_tile, int split) {
+  using T = __nv_bfloat16;
+  constexpr int CH = TcCfg<BN>::kChunk < 64 ? TcCfg<BN>::kChunk : 64;  // <= 8 prefetched vectors per thread
+  constexpr int KU = CH / 8;   // (token, 8-row) units per thread per chunk
+  constexpr int KG = CH / 16;  // gelu units per thread per chunk
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, e = threadIdx.x - 64, q = warp & 3;
+  const int n_base = m_tile * 128;
+  const int t_tile = n_tile * BN;
+  const int kind = P.kind;
+  const bool aux_kind = kind == EPI_HXPRE || kind == EPI_XMOE;
+  pdl_wait();
+  // ---- prefetch (independent of the accumulator)
+  const int c8 = e & 15, n0 = n_base + c8 * 8;
+  const bool v8 = n0 < P.Nw;
+  float b8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (kind != EPI_GELU_UP && kind != EPI_ARGMAX && kind != EPI_PARTIAL && P.bias && v8)
+    load8(reinterpret_cast<const T*>(P.bias) + n0, b8);
+  const int cg = e & 7, ng = n_base + cg * 16;
+  float bg[16] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+  if (kind == EPI_GELU_UP && P.bias && ng < P.Nw) {
+    load8(reinterpret_cast<const T*>(P.bias) + ng, bg);
+    load8(reinterpret_cast<const T*>(P.bias) + ng + 8, bg + 8);
+  }
+  uint4 auxr[KU];
+  auto aux_load = [&](int cc) {
+#pragma unroll
+    for (int k = 0; k < KU; ++k) {
+      const int t = t_tile + cc + (e >> 4) + 8 * k;
+      auxr[k] = make_uint4(0, 0, 0, 0);
+      if (aux_kind && v8 && t < P.T && (e >> 4) + 8 * k < CH)
+        auxr[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0);
+    }
+  };
+  aux_load(0);
+  const bool ok = mbar_wait(accb, 0, p.err, 3);
+  tc_fence_after();
+  for (int cc = 0; cc < BN; cc += CH) {
+    const int tn = min(CH, P.T - (t_tile + cc));
+    if (tn <= 0) break;
+    if (cc > 0) aux_load(cc);
+    // ---- E1
+    if (kind == EPI_ARGMAX) {
+      // per token: max over this warp's 32 rows of a 32-bit key (order-preserving bf16 bits,
+      // then 255 - row in tile, so equal values keep the lowest row), one redux per token;
+      // the four warps' keys meet in S, then one 64-bit atomicMax per token and CTA.
+      uint32_t* K = reinterpret_cast<uint32_t*>(S);  // [4 warps][CH tokens]
+      const int nrow = n_base + q * 32 + lane;
+      const int nl = q * 32 + lane;
+      T* out = reinterpret_cast<T*>(P.out);
+      if (ok)
+        for (int c0 = 0; c0 < CH; c0 += 16) {
+          if (c0 >= tn) break;  // warp-uniform
+          float v[16];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc + c0), v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            uint32_t key = 0u;
+            if (nrow < P.Nw) {
+              uint32_t b = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
+              b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+              key = (b << 8) | (uint32_t)(255 - nl);
+              if (out && c0 + j < tn) st<T>(out + (size_t)(t_tile + cc + c0 + j) * P.ldo + nrow, v[j]);
+            }
+            key = __reduce_max_sync(0xffffffffu, key);
+            if (lane == 0) K[q * CH + c0 + j] = key;
+          }
+        }
+      named_barrier_sync(1, 128);
+      for (int tl = e; tl < tn; tl += 128) {
+        uint32_t best = 0u;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) best = max(best, K[w * CH + tl]);
+        if (best) {
+          const int n = n_base + 255 - (int)(best & 0xFFu);
+          const uint32_t b = best >> 8;
+          atomicMax(P.best + t_tile + cc + tl,
+                    ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n));
+        }
+      }
+      named_barrier_sync(1, 128);
+      continue;
+    }
+    if (ok)
+      for (int c0 = 0; c0 < CH; c0 += 16) {
+        if (c0 >= tn) break;  // warp-uniform
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc + c0), v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
+      }
+    named_barrier_sync(1, 128);
+    // ---- E2
+    const int tb = t_tile + cc;
+    if (false) {
+    } else if (kind == EPI_GELU_UP) {
+      T* out = reinterpret_cast<T*>(P.out);
+#pragma unroll
+      for (int k = 0; k < KG; ++k) {
+        const int tl = (e >> 3) + 16 * k;
+        if (tl >= tn || ng >= P.Nw) continue;
+        const float* sv = S + tl * 128 + cg * 16;
+        float o8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float gb = rnd<T>(sv[2 * j] + bg[2 * j]);
+          const float ub = rnd<T>(sv[2 * j + 1] + bg[2 * j + 1]);
+          o8[j] = rnd<T>(gelu_erf(gb)) * ub;
+        }
+        store8(out + (size_t)(tb + tl) * P.ldo + (ng >> 1), o8);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < KU; ++k) {
+        const int tl = (e >> 4) + 8 * k;
+        if (tl >= tn || !v8) continue;
+        const int t = tb + tl;
+        float a[8];
+        {
+          const float4 f0 = *reinterpret_cast<const float4*>(S + tl * 128 + c8 * 8);
+          const float4 f1 = *reinterpret_cast<const float4*>(S + tl * 128 + c8 * 8 + 4);
+          a[0] = f0.x; a[1] = f0.y; a[2] = f0.z; a[3] = f0.w; a[4] = f1.x; a[5] = f1.y; a[6] = f1.z; a[7] = f1.w;
+        }
+        if (kind == EPI_PARTIAL) {
+          store8(P.ws + ((size_t)split * P.T + t) * P.ldw + n0, a);
+          continue;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] += b8[j];
+        T* out = reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n0;
+        if (kind == EPI_STORE) {
+          store8(out, a);
+        } else if (kind == EPI_CX) {
+          float y[8], z[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            y[j] = rnd<T>(a[j]);
+            z[j] = fminf(fmaxf(y[j], -1e4f), 1e4f);
+          }
+          store8(out, y);
+          store8(reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0, z);
+        } else {  // HXPRE: aux + clamp(y); XMOE: aux * clamp(y)
+          float x[8], y[8];
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&auxr[k]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h2[j]);
+            x[2 * j] = f.x;
+            x[2 * j + 1] = f.y;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float cl = fminf(fmaxf(rnd<T>(a[j]), -100.f), 100.f);
+            y[j] = kind == EPI_HXPRE ? x[j] + cl : x[j] * cl;
+          }
+          store8(out, y);
+        }
+      }
+    }
+    named_barrier_sync(1, 128);
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -358,35 +532,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tc_kernel(const __grid_const
       umma_commit(accb);
     }
   }
-  // ---------------- epilogue
-  // E1: warps 2..5 (TMEM lane quarter = warp % 4) move the accumulator into a shared fp32
-  //     staging tile S[token][row] (BN x 128), reusing the pipeline buffers: every MMA,
-  //     and so every read of those buffers, has completed once accb fires.
-  // E2: all six warps apply the epilogue on 8-wide row vectors and store 16-byte chunks.
-  float* S = reinterpret_cast<float*>(smem);
-  pdl_wait();
-  bool ok = true;
-  if (warp >= 2) {
-    ok = mbar_wait(accb, 0, p.err, 3);
-    tc_fence_after();
-  }
-  for (int cc = 0; cc < BN; cc += C::kChunk) {
-    if (warp >= 2 && ok) {
-      const int q = warp & 3;
-      for (int c0 = 0; c0 < C::kChunk; c0 += 16) {
-        if (n_tile * BN + cc + c0 >= P.T) break;  // warp-uniform
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc + c0), v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
-      }
-    }
-    __syncthreads();
-    const int t_base = n_tile * BN + cc;
-    epilogue_tile<__nv_bfloat16>(P, S, m_tile * 128, t_base, min(C::kChunk, P.T - t_base), split, C::kThreads);
-    __syncthreads();
-  }
+  // ---------------- epilogue (warps 2..5 only; warps 0..1 go straight to teardown)
+  if (warp >= 2) tc_epilogue<BN>(p, P, reinterpret_cast<float*>(smem), tmem, accb, m_tile, n_tile, split);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
