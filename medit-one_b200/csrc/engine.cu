@@ -486,7 +486,7 @@ static int check_cfg(const one_config& c) {
     return fail(ONE_ERR_UNSUPPORTED, "transformer_dim must be a multiple of 8 and <= 1024");
   if (c.num_attention_heads * c.head_dim != c.transformer_dim)
     return fail(ONE_ERR_UNSUPPORTED, "num_attention_heads * head_dim must equal transformer_dim");
-  if (c.head_dim % 2 || c.head_dim > 256) return fail(ONE_ERR_UNSUPPORTED, "head_dim must be even and <= 256");
+  if (c.head_dim % 16 || c.head_dim > 256) return fail(ONE_ERR_UNSUPPORTED, "head_dim must be a multiple of 16, <= 256");
   if (c.num_attention_heads > 64) return fail(ONE_ERR_UNSUPPORTED, "at most 64 heads");
   if (c.num_experts < 0 || c.num_experts > kMaxExperts) return fail(ONE_ERR_UNSUPPORTED, "at most %d experts", kMaxExperts);
   if (c.num_experts > 0 && (c.top_k < 1 || c.r < 1)) return fail(ONE_ERR_INVALID, "top_k and r must be positive");

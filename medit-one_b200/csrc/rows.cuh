@@ -460,10 +460,10 @@ __host__ __device__ inline AttnLayout attn_layout(int H, int Dh, int r, int E, i
   AttnLayout L;
   int off = 0;
   const int HD = H * Dh, HH = H * H, Dp = Dh + 4;
-  L.wqkv = attn_take(off, 3 * H * Dp * 4);
+  L.wqkv = attn_take(off, (es == 4 || H > 16) ? 3 * H * Dp * 4 : 0);  // CUDA-core projections only
   L.bqkv = attn_take(off, 3 * H * 4);
   L.gate_ld = HH + (es == 2 ? 2 : 1);  // odd row stride in 32-bit words: conflict-free rows
-  L.gate = attn_take(off, use_moe ? 2 * r * L.gate_ld * es : 0);
+  L.gate = attn_take(off, 0);  // the router weights are read where they are used (L1/L2)
   L.experts = attn_take(off, use_moe ? 3 * E * 4 : 0);
   L.b2 = attn_take(off, use_moe ? E * (2 * HH + D) * es : 0);
   L.tok0 = off;
@@ -487,6 +487,20 @@ __host__ __device__ inline AttnLayout attn_layout(int H, int Dh, int r, int E, i
   L.total = off + kAttnTok * t;
   return L;
 }
+
+// D += A * B for one m16n8k16 tile, bf16 inputs, fp32 accumulators (warp-wide).
+ONE_DEVINL void mma_16816_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+ONE_DEVINL uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+ONE_DEVINL uint32_t ldg_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 ONE_DEVINL void named_bar(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 
@@ -581,41 +595,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttn
   const AttnLayout L = attn_layout(H, Dh, r, E, D, p.use_moe, (int)sizeof(T));
   float* wqkv = reinterpret_cast<float*>(smb + L.wqkv);
   float* bqkv = reinterpret_cast<float*>(smb + L.bqkv);
-  T* gate = reinterpret_cast<T*>(smb + L.gate);
   float* exps = reinterpret_cast<float*>(smb + L.experts);
-  T* b2s = reinterpret_cast<T*>(smb + L.b2);
   const int half = Dh / 2, Dp = Dh + 4;
   const int inr[3] = {HH, HH, D};
-  const int b2off[3] = {0, E * HH, 2 * E * HH};
 
-  // ---- weights to shared memory (not written by the previous kernel: before the wait)
-  for (int v = tid; v < 3 * HD / 8; v += nthr) {
-    const int u = (v * 8) / Dh, d0 = (v * 8) % Dh, which = u / H;
-    const T* W = reinterpret_cast<const T*>(which == 0 ? p.wq : which == 1 ? p.wk : p.wv);
-    float x[8];
-    load8(W + (size_t)(u % H) * Dh + d0, x);
+  // ---- small weights to shared memory (not written by the previous kernel: before the wait)
+  constexpr bool kTensor = sizeof(T) == 2;  // bf16: projections and gates on mma.sync
+  if (!kTensor || H > 16)
+    for (int v = tid; v < 3 * HD / 8; v += nthr) {
+      const int u = (v * 8) / Dh, d0 = (v * 8) % Dh, which = u / H;
+      const T* W = reinterpret_cast<const T*>(which == 0 ? p.wq : which == 1 ? p.wk : p.wv);
+      float x[8];
+      load8(W + (size_t)(u % H) * Dh + d0, x);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) wqkv[u * Dp + d0 + e] = x[e];
-  }
+      for (int e = 0; e < 8; ++e) wqkv[u * Dp + d0 + e] = x[e];
+    }
   for (int i = tid; i < 3 * H; i += nthr) {
     const int which = i / H, j = i % H;
     const T* Bb = reinterpret_cast<const T*>(which == 0 ? p.bq : which == 1 ? p.bk : p.bv);
     bqkv[i] = ld<T>(Bb + j);
   }
+  T* b2s = reinterpret_cast<T*>(smb + L.b2);
+  const int b2off[3] = {0, E * HH, 2 * E * HH};
   if (p.use_moe) {
-    const int wpr = HH * (int)sizeof(T) / 4, wld = L.gate_ld * (int)sizeof(T) / 4;
-    for (int w = tid; w < 2 * r * wpr; w += nthr) {
-      const int j = w / wpr, c = w % wpr, ri = j / r;
-      reinterpret_cast<uint32_t*>(gate)[j * wld + c] = reinterpret_cast<const uint32_t*>(p.rt[ri].gate_w)[(j % r) * wpr + c];
-    }
+    for (int i = tid; i < 3 * E; i += nthr)
+      exps[i] = fminf(fmaxf(ld<T>(reinterpret_cast<const T*>(p.rt[i / E].experts) + i % E), -10.f), 10.f);
     constexpr int VE = 16 / (int)sizeof(T);
     for (int ri = 0; ri < 3; ++ri) {
       const uint4* src = reinterpret_cast<const uint4*>(p.rt[ri].bias2);
       uint4* dst = reinterpret_cast<uint4*>(b2s + b2off[ri]);
       for (int v = tid; v < E * inr[ri] / VE; v += nthr) dst[v] = src[v];
     }
-    for (int i = tid; i < 3 * E; i += nthr)
-      exps[i] = fminf(fmaxf(ld<T>(reinterpret_cast<const T*>(p.rt[i / E].experts) + i % E), -10.f), 10.f);
   }
   if (tid == 0) pdl_launch_dependents();
   pdl_wait();
@@ -662,8 +672,123 @@ __global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttn
     }
     __syncthreads();
 
-    // ---- phase A: one warp per (token, head)
-    for (int pr_ = warp; pr_ < ntok * H; pr_ += nw) {
+    // ---- phase A
+    const bool mmaA = kTensor && H <= 16;
+    if (mmaA) {
+      // warp per head, both tokens at once: RoPE into shared rows, then q|k|v = x @ W^T on
+      // mma.sync (the tokens are the M rows of an m16n8k16 tile), bias, rounding, softmax.
+      for (int h = warp; h < H; h += nw) {
+        for (int k = 0; k < ntok; ++k) {
+          uint8_t* tb = smb + L.tok0 + k * L.tk.bytes;
+          const float* row = reinterpret_cast<const float*>(tb + L.tk.row);
+          const float* cs = reinterpret_cast<const float*>(tb + L.tk.cs);
+          float* xr = reinterpret_cast<float*>(tb + L.tk.rot) + h * 2 * Dp;
+          float* kr = xr + Dp;
+          const float* sx = row + h * Dh;
+          const float* sk = row + HD + h * Dh;
+          for (int d = lane; d < Dh; d += 32) {
+            const float px = d < half ? -sx[d + half] : sx[d - half];
+            const float pk = d < half ? -sk[d + half] : sk[d - half];
+            xr[d] = rnd<T>(rnd<T>(sx[d] * cs[d]) + rnd<T>(px * cs[Dh + d]));
+            kr[d] = rnd<T>(rnd<T>(sk[d] * cs[d]) + rnd<T>(pk * cs[Dh + d]));
+          }
+        }
+        __syncwarp();
+        const int g = lane >> 2, c = lane & 3;
+        const bool rowok = g < ntok;
+        const float* srcs[3] = {nullptr, nullptr, nullptr};
+        if (rowok) {
+          uint8_t* tb = smb + L.tok0 + g * L.tk.bytes;
+          float* xr = reinterpret_cast<float*>(tb + L.tk.rot) + h * 2 * Dp;
+          srcs[0] = xr;
+          srcs[1] = xr + Dp;
+          srcs[2] = reinterpret_cast<const float*>(tb + L.tk.row) + 2 * HD + h * Dh;
+        }
+        const T* Ws[3] = {reinterpret_cast<const T*>(p.wq), reinterpret_cast<const T*>(p.wk), reinterpret_cast<const T*>(p.wv)};
+        float acc[3][2][4];
+#pragma unroll
+        for (int pj = 0; pj < 3; ++pj)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[pj][nt][q] = 0.f;
+        for (int ks = 0; ks < Dh; ks += 16) {
+#pragma unroll
+          for (int pj = 0; pj < 3; ++pj) {
+            uint32_t a[4] = {0u, 0u, 0u, 0u};
+            if (rowok) {
+              a[0] = pack_bf16(srcs[pj][ks + 2 * c], srcs[pj][ks + 2 * c + 1]);
+              a[2] = pack_bf16(srcs[pj][ks + 2 * c + 8], srcs[pj][ks + 2 * c + 9]);
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              const int n = nt * 8 + g;
+              uint32_t b0 = 0u, b1 = 0u;
+              if (n < H) {
+                const T* wr = Ws[pj] + (size_t)n * Dh + ks + 2 * c;
+                b0 = ldg_u32(wr);
+                b1 = ldg_u32(wr + 8);
+              }
+              mma_16816_bf16(acc[pj][nt], a, b0, b1);
+            }
+          }
+        }
+        // lane (g, c) holds token g's outputs j = nt * 8 + 2c + {0, 1}
+        float lg[4], vv[4];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int nt = q >> 1, j = nt * 8 + 2 * c + (q & 1);
+          lg[q] = -INFINITY;
+          vv[q] = 0.f;
+          if (rowok && j < H) {
+            const float qv = rnd<T>(acc[0][nt][q & 1] + bqkv[j]);
+            const float kv = rnd<T>(acc[1][nt][q & 1] + bqkv[H + j]);
+            vv[q] = rnd<T>(acc[2][nt][q & 1] + bqkv[2 * H + j]);
+            lg[q] = rnd<T>(qv * kv);
+            mx = fmaxf(mx, lg[q]);
+          }
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        float m2 = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (lg[q] != -INFINITY) {
+            lg[q] = rnd<T>(lg[q] - mx);
+            m2 = fmaxf(m2, lg[q]);
+          }
+        m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
+        m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, 2));
+        float ex[4], sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          ex[q] = lg[q] != -INFINITY ? expf(lg[q] - m2) : 0.f;
+          sum += ex[q];
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (rowok) {
+          uint8_t* tb = smb + L.tok0 + g * L.tk.bytes;
+          float* o = reinterpret_cast<float*>(tb + L.tk.o);
+          float* xs = reinterpret_cast<float*>(tb + L.tk.xs);
+          const float inv = 1.0f / sum;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int j = (q >> 1) * 8 + 2 * c + (q & 1);
+            if (j < H) {
+              float w = ex[q] * inv;
+              w = isnan(w) ? 1.0f / (float)H : rnd<T>(w);
+              const float ov = rnd<T>(w * vv[q]);
+              o[h * H + j] = ov;
+              xs[h * H + j] = fminf(fmaxf(ov, -1e4f), 1e4f);  // LinearMoE clamp (:53)
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+    for (int pr_ = warp; !mmaA && pr_ < ntok * H; pr_ += nw) {
       const int k = pr_ / H, h = pr_ % H;
       uint8_t* tb = smb + L.tok0 + k * L.tk.bytes;
       const float* row = reinterpret_cast<const float*>(tb + L.tk.row);
@@ -685,17 +810,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttn
         const int which = u / H;
         const float* src = which == 0 ? xr : which == 1 ? kr : sv;
         const float* w = wqkv + u * Dp;
-        float acc = 0.f;
+        // four independent partial sums over 16-wide slices, added in slice order
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
         if (which < 2) {
-          for (int d = 0; d < Dh; d += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(w + d);
-            const float4 b = *reinterpret_cast<const float4*>(src + d);
-            acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc); acc = fmaf(a.z, b.z, acc); acc = fmaf(a.w, b.w, acc);
+#pragma unroll 2
+          for (int d = 0; d < Dh; d += 16) {
+            const float4 w0 = *reinterpret_cast<const float4*>(w + d), x0 = *reinterpret_cast<const float4*>(src + d);
+            const float4 w1 = *reinterpret_cast<const float4*>(w + d + 4), x1 = *reinterpret_cast<const float4*>(src + d + 4);
+            const float4 w2 = *reinterpret_cast<const float4*>(w + d + 8), x2 = *reinterpret_cast<const float4*>(src + d + 8);
+            const float4 w3 = *reinterpret_cast<const float4*>(w + d + 12), x3 = *reinterpret_cast<const float4*>(src + d + 12);
+            a0 = fmaf(w0.x, x0.x, a0); a0 = fmaf(w0.y, x0.y, a0); a0 = fmaf(w0.z, x0.z, a0); a0 = fmaf(w0.w, x0.w, a0);
+            a1 = fmaf(w1.x, x1.x, a1); a1 = fmaf(w1.y, x1.y, a1); a1 = fmaf(w1.z, x1.z, a1); a1 = fmaf(w1.w, x1.w, a1);
+            a2 = fmaf(w2.x, x2.x, a2); a2 = fmaf(w2.y, x2.y, a2); a2 = fmaf(w2.z, x2.z, a2); a2 = fmaf(w2.w, x2.w, a2);
+            a3 = fmaf(w3.x, x3.x, a3); a3 = fmaf(w3.y, x3.y, a3); a3 = fmaf(w3.z, x3.z, a3); a3 = fmaf(w3.w, x3.w, a3);
           }
         } else {
-          for (int d = 0; d < Dh; ++d) acc = fmaf(w[d], src[d], acc);
+#pragma unroll 4
+          for (int d = 0; d < Dh; d += 4) {
+            a0 = fmaf(w[d], src[d], a0);
+            a1 = fmaf(w[d + 1], src[d + 1], a1);
+            a2 = fmaf(w[d + 2], src[d + 2], a2);
+            a3 = fmaf(w[d + 3], src[d + 3], a3);
+          }
         }
-        qh[u] = rnd<T>(acc + bqkv[u]);
+        qh[u] = rnd<T>(((a0 + a1) + (a2 + a3)) + bqkv[u]);
       }
       __syncwarp();
       float lg = -INFINITY, v = 0.f;
@@ -724,6 +862,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttn
         for (int i = tid; i < HH; i += nthr) st<T>(O + i, o[i]);
       }
     }
+    if (p.use_moe && kTensor && HH % 16 == 0) {
+      // ---- gate logits of hx_moe / x_moe (:56) on clamp(o): [tokens x HH] @ [HH x 2r] on
+      // mma.sync, a warp per 8 gate rows, rounded to the dtype
+      const int g = lane >> 2, c = lane & 3;
+      for (int nt = warp; nt < 2 * r / 8; nt += nw) {
+        const int ri = (nt * 8) / r, j0 = nt * 8 - ri * r;
+        const T* W = reinterpret_cast<const T*>(p.rt[ri].gate_w) + (size_t)(j0 + g) * HH + 2 * c;
+        const float* xs = g < ntok ? reinterpret_cast<const float*>(smb + L.tok0 + g * L.tk.bytes + L.tk.xs) : nullptr;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int ks = 0; ks < HH; ks += 16) {
+          uint32_t a[4] = {0u, 0u, 0u, 0u};
+          if (xs) {
+            a[0] = pack_bf16(xs[ks + 2 * c], xs[ks + 2 * c + 1]);
+            a[2] = pack_bf16(xs[ks + 2 * c + 8], xs[ks + 2 * c + 9]);
+          }
+          mma_16816_bf16(acc, a, ldg_u32(W + ks), ldg_u32(W + ks + 8));
+        }
+        if (xs) {
+          float* gl = reinterpret_cast<float*>(smb + L.tok0 + g * L.tk.bytes + L.tk.gl) + ri * r;
+          gl[j0 + 2 * c] = rnd<T>(acc[0]);
+          gl[j0 + 2 * c + 1] = rnd<T>(acc[1]);
+        }
+      }
+      __syncthreads();
+    }
     if (p.use_moe) {
       // ---- phase B: routers, warps grouped per token slot (6 warps each)
       const int k = warp / 6, role = warp % 6;
@@ -742,12 +905,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttn
           // hx_moe (role 0) / x_moe (role 1) on clamp(o)
           const int ri = role;
           float* g = gl + ri * r;
-          const T* Wg = gate + (size_t)ri * r * L.gate_ld;
-          for (int j = lane; j < r; j += 32) {
-            const T* wr = Wg + j * L.gate_ld;
-            float acc = 0.f;
-            for (int i = 0; i < HH; ++i) acc = fmaf(ld<T>(wr + i), xs[i], acc);
-            g[j] = rnd<T>(acc);  // gate logits (:56)
+          const T* Wg = reinterpret_cast<const T*>(p.rt[ri].gate_w);
+          for (int j = lane; j < r && !(kTensor && HH % 16 == 0); j += 32) {
+            const T* wr = Wg + j * HH;
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            int i = 0;
+#pragma unroll 2
+            for (; i + 4 <= HH; i += 4) {
+              a0 = fmaf(ld<T>(wr + i), xs[i], a0);
+              a1 = fmaf(ld<T>(wr + i + 1), xs[i + 1], a1);
+              a2 = fmaf(ld<T>(wr + i + 2), xs[i + 2], a2);
+              a3 = fmaf(ld<T>(wr + i + 3), xs[i + 3], a3);
+            }
+            for (; i < HH; ++i) a0 = fmaf(ld<T>(wr + i), xs[i], a0);
+            g[j] = rnd<T>((a0 + a1) + (a2 + a3));  // gate logits (:56)
           }
           __syncwarp();
           float* c = cvb + ri * E;
