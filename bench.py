@@ -310,6 +310,26 @@ def run_native(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def profile_case(args):
+    """Small fixed case for ncu captures: 140M engine at batch 256, a 16-token prompt, then
+    three graph-replayed decode steps (launch order: prompt kernels, then 76 per step)."""
+    from one.configuration_one import config_140m
+    from one.engine import OneEngine
+    from one.initialization import init_state_dict
+    cfg = config_140m()
+    eng = OneEngine(cfg, init_state_dict(cfg, SEED, torch.bfloat16), "cuda", torch.bfloat16, max_batch=BATCH,
+                    max_tokens=BATCH * 16)
+    g = torch.Generator().manual_seed(SEED)
+    eng.prefill(torch.randint(0, cfg.vocab_size, (BATCH, 16), generator=g).cuda())
+    eng.capture(1)
+    for _ in range(3):
+        eng.replay()
+    torch.cuda.synchronize()
+    if eng.device_error() != (0, 0):
+        raise RuntimeError(f"device error {eng.device_error()}")
+    print(json.dumps({"profile_case": "ok", "launches_per_step": eng.step_launches(BATCH)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -317,7 +337,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args)
+        return
     if args.impl == "reference":
         # rank 0 alone times the host-CPU reference; other ranks exit without work
         if int(os.environ.get("RANK", "0")) == 0:
