@@ -187,6 +187,22 @@ int one_combined_rope_attention(const void* single_x, const void* key, const voi
 int one_flash_attention(const void* q, const void* k, const void* v, int32_t b, int32_t h, int32_t nq, int32_t nk,
                         int32_t dh, int32_t causal, float scale, int32_t dtype, void* out, void* stream);
 
+/* The RoPE + attention operator of the isolated attention workload: apply_rotary_pos_emb_flash
+ * (one/flash_attention.py:26-33) on q and k with cos, sin [cos_batch, n, dh] (cos_batch = b, or
+ * 1 when shared by the batch), then exact softmax attention as one_flash_attention. q, k, v,
+ * out [b, h, n, dh]. The workspace holds the rotated q and k (no reference counterpart: the
+ * reference applies RoPE and attention as two Python calls). */
+size_t one_rope_flash_attention_workspace_bytes(int32_t b, int32_t h, int32_t n, int32_t dh, int32_t dtype);
+int one_rope_flash_attention(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+                             int32_t cos_batch, int32_t b, int32_t h, int32_t n, int32_t dh, int32_t causal, float scale,
+                             int32_t dtype, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Error record of the standalone ops' kernels: a bounded device-side wait that ran out
+ * records its code and site here instead of trapping. Returns the code (0 = none) and the
+ * site in *where (may be NULL); clears the record when clear != 0. Synchronises the device.
+ * (No reference counterpart: the reference's kernels have no device-side waits.) */
+int one_ops_error(int32_t* where, int32_t clear);
+
 #ifdef __cplusplus
 }
 #endif

@@ -142,18 +142,167 @@ extern "C" int one_combined_rope_attention(const void* single_x, const void* key
   return ONE_OK;
 }
 
-extern "C" int one_flash_attention(const void* q, const void* k, const void* v, int32_t b, int32_t h, int32_t nq, int32_t nk,
-                                   int32_t dh, int32_t causal, float scale, int32_t dtype, void* out, void* stream) {
-  if (!q || !k || !v || !out || b < 1 || h < 1 || nq < 1 || nk < 1 || dh < 1 || dh > 64)
-    return fail(ONE_ERR_INVALID, "bad attention arguments");
-  cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid((nq + 63) / 64, b * h);
-  cudaError_t e = dtype == ONE_DTYPE_BF16
-                      ? launch_k(attn_simt_kernel<__nv_bfloat16>, grid, dim3(64), 0, st, (const __nv_bfloat16*)q,
-                                 (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (int)nq, (int)nk, (int)dh, (int)causal,
-                                 scale, (__nv_bfloat16*)out)
-                      : launch_k(attn_simt_kernel<float>, grid, dim3(64), 0, st, (const float*)q, (const float*)k,
-                                 (const float*)v, (int)nq, (int)nk, (int)dh, (int)causal, scale, (float*)out);
+// ------------------------------------------------------------------ attention
+// Error record shared by the standalone ops' kernels (bounded waits that ran out).
+__device__ DevErr g_ops_err;
+static DevErr* ops_err_ptr() {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev] && cudaGetSymbolAddress(&addr[dev], g_ops_err) != cudaSuccess) addr[dev] = nullptr;
+  return reinterpret_cast<DevErr*>(addr[dev]);
+}
+
+extern "C" int one_ops_error(int32_t* where, int32_t clear) {
+  DevErr h{0, 0};
+  CK(cudaDeviceSynchronize());
+  CK(cudaMemcpyFromSymbol(&h, g_ops_err, sizeof(h)));
+  if (clear) {
+    const DevErr z{0, 0};
+    CK(cudaMemcpyToSymbol(g_ops_err, &z, sizeof(z)));
+  }
+  if (where) *where = h.where;
+  return h.code;
+}
+
+// bf16 3-D map over [bh][n][64] rows: box {64, 128, 1}, 128-byte swizzle, zero fill past n.
+static int make_map_bhn(CUtensorMap* m, const void* ptr, int bh, int n) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ONE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (reinterpret_cast<uintptr_t>(ptr) & 15) return fail(ONE_ERR_INVALID, "attention operands must be 16-byte aligned");
+  cuuint64_t dims[3] = {(cuuint64_t)kFaDh, (cuuint64_t)n, (cuuint64_t)bh};
+  cuuint64_t strides[2] = {(cuuint64_t)kFaDh * 2, (cuuint64_t)n * kFaDh * 2};
+  cuuint32_t box[3] = {(cuuint32_t)kFaDh, (cuuint32_t)kFaRows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ONE_ERR_CUDA, "cuTensorMapEncodeTiled (attention) failed (%d)", (int)r);
+  return ONE_OK;
+}
+
+// The tensor-core kernel: bf16, head_dim 64, 16-byte aligned operands, and a positive
+// scale (it takes the row max before scaling).
+static bool attn_tc_eligible(const void* q, const void* k, const void* v, const void* out, int dh, float scale,
+                             int dtype) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                      reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
+  return dtype == ONE_DTYPE_BF16 && dh == kFaDh && (a & 15) == 0 && scale > 0.f && scale < 3.0e38f;
+}
+
+static int attn_launch(const void* q, const void* k, const void* v, int b, int h, int nq, int nk, int dh, int causal,
+                       float scale, int dtype, void* out, cudaStream_t st) {
+  cudaError_t e;
+  if (attn_tc_eligible(q, k, v, out, dh, scale, dtype)) {
+    int rc = set_kernel_attrs();
+    if (rc) return rc;
+    FaParams p;
+    memset(&p, 0, sizeof(p));
+    const int bh = b * h;
+    if ((rc = make_map_bhn(&p.tq, q, bh, nq)) || (rc = make_map_bhn(&p.tk, k, bh, nk)) ||
+        (rc = make_map_bhn(&p.tv, v, bh, nk)))
+      return rc;
+    p.out = (__nv_bfloat16*)out;
+    p.nq = nq;
+    p.nk = nk;
+    p.causal = causal ? 1 : 0;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.err = ops_err_ptr();
+    static int resident = -1;
+    if (resident < 0) {
+      CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, flash_attn_tc_kernel, kFaThreads, kFaSmem));
+    }
+    if (resident < 1) return fail(ONE_ERR_CUDA, "attention kernel does not fit on an SM (registers / shared memory)");
+    const int pairs = (nq + kFaRows * kFaQTiles - 1) / (kFaRows * kFaQTiles);
+    if (pairs > 65535) return fail(ONE_ERR_UNSUPPORTED, "attention: nq too large");
+    e = launch_k(flash_attn_tc_kernel, dim3(bh, pairs), dim3(kFaThreads), kFaSmem, st, p);
+  } else {
+    if (dh > 64) return fail(ONE_ERR_UNSUPPORTED, "attention: head_dim <= 64 (tensor-core path: bf16, head_dim 64)");
+    dim3 grid((nq + 63) / 64, b * h);
+    e = dtype == ONE_DTYPE_BF16
+            ? launch_k(attn_simt_kernel<__nv_bfloat16>, grid, dim3(64), 0, st, (const __nv_bfloat16*)q,
+                       (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, nq, nk, dh, causal, scale, (__nv_bfloat16*)out)
+            : launch_k(attn_simt_kernel<float>, grid, dim3(64), 0, st, (const float*)q, (const float*)k,
+                       (const float*)v, nq, nk, dh, causal, scale, (float*)out);
+  }
   if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return ONE_OK;
+}
+
+extern "C" int one_flash_attention(const void* q, const void* k, const void* v, int32_t b, int32_t h, int32_t nq, int32_t nk,
+                                   int32_t dh, int32_t causal, float scale, int32_t dtype, void* out, void* stream) {
+  if (!q || !k || !v || !out || b < 1 || h < 1 || nq < 1 || nk < 1 || dh < 1)
+    return fail(ONE_ERR_INVALID, "bad attention arguments");
+  if ((long)b * h > 0x7fffffffL) return fail(ONE_ERR_UNSUPPORTED, "attention: b * h too large");
+  return attn_launch(q, k, v, b, h, nq, nk, dh, causal, scale, dtype, out, (cudaStream_t)stream);
+}
+
+// x * cos + rotate_half(x) * sin for any dtype / even head_dim: one thread per element pair.
+template <typename T>
+__global__ void rope_qk_generic_kernel(const T* q, const T* k, const T* cosv, const T* sinv, int h, int n, int dh,
+                                       long cs_bstride, long rows, T* qr, T* kr) {
+  pdl_wait();
+  const int half = dh / 2;
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * 2 * half) return;
+  const int e = (int)(i % half);
+  long row = i / half;
+  const bool is_k = row >= rows;
+  if (is_k) row -= rows;
+  const long bhi = row / n;
+  const int pos = (int)(row - bhi * n);
+  const long b = bhi / h;
+  const T* x = (is_k ? k : q) + row * dh;
+  const T* cs = cosv + b * cs_bstride + (long)pos * dh;
+  const T* sn = sinv + b * cs_bstride + (long)pos * dh;
+  const float x1 = ld<T>(x + e), x2 = ld<T>(x + half + e);
+  T* y = (is_k ? kr : qr) + row * dh;
+  st<T>(y + e, rnd<T>(x1 * ld<T>(cs + e)) + rnd<T>(-x2 * ld<T>(sn + e)));
+  st<T>(y + half + e, rnd<T>(x2 * ld<T>(cs + half + e)) + rnd<T>(x1 * ld<T>(sn + half + e)));
+}
+
+extern "C" size_t one_rope_flash_attention_workspace_bytes(int32_t b, int32_t h, int32_t n, int32_t dh, int32_t dtype) {
+  const size_t es = dtype == ONE_DTYPE_F32 ? 4 : 2;
+  return 2 * align1k((size_t)b * h * n * dh * es) + 1024;
+}
+
+extern "C" int one_rope_flash_attention(const void* q, const void* k, const void* v, const void* cosv, const void* sinv,
+                                        int32_t cos_batch, int32_t b, int32_t h, int32_t n, int32_t dh, int32_t causal,
+                                        float scale, int32_t dtype, void* out, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+  if (!q || !k || !v || !cosv || !sinv || !out || !workspace || b < 1 || h < 1 || n < 1 || dh < 2 || (dh & 1))
+    return fail(ONE_ERR_INVALID, "bad RoPE attention arguments");
+  if (cos_batch != 1 && cos_batch != b) return fail(ONE_ERR_INVALID, "cos_batch must be 1 or b");
+  if (workspace_bytes < one_rope_flash_attention_workspace_bytes(b, h, n, dh, dtype))
+    return fail(ONE_ERR_INVALID, "workspace too small");
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t es = dtype == ONE_DTYPE_F32 ? 4 : 2;
+  uint8_t* ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(workspace) + 1023) & ~uintptr_t(1023));
+  void* qr = ws;
+  void* kr = ws + align1k((size_t)b * h * n * dh * es);
+  const long rows = (long)b * h * n;
+  const long cs_bstride = cos_batch == 1 ? 0 : (long)n * dh;
+  cudaError_t e;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                       reinterpret_cast<uintptr_t>(cosv) | reinterpret_cast<uintptr_t>(sinv);
+  if (dtype == ONE_DTYPE_BF16 && dh == 64 && (al & 15) == 0) {
+    const long threads = rows * 8;
+    e = launch_k(rope_qk_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, (const __nv_bfloat16*)q,
+                 (const __nv_bfloat16*)k, (const __nv_bfloat16*)cosv, (const __nv_bfloat16*)sinv, (int)h, (int)n,
+                 cs_bstride, rows, (__nv_bfloat16*)qr, (__nv_bfloat16*)kr);
+  } else {
+    const long threads = rows * dh;
+    const dim3 grid((unsigned)((threads + 255) / 256));
+    e = dtype == ONE_DTYPE_BF16
+            ? launch_k(rope_qk_generic_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, (const __nv_bfloat16*)q,
+                       (const __nv_bfloat16*)k, (const __nv_bfloat16*)cosv, (const __nv_bfloat16*)sinv, (int)h, (int)n,
+                       (int)dh, cs_bstride, rows, (__nv_bfloat16*)qr, (__nv_bfloat16*)kr)
+            : launch_k(rope_qk_generic_kernel<float>, grid, dim3(256), 0, st, (const float*)q, (const float*)k,
+                       (const float*)cosv, (const float*)sinv, (int)h, (int)n, (int)dh, cs_bstride, rows, (float*)qr,
+                       (float*)kr);
+  }
+  if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "RoPE launch: %s", cudaGetErrorString(e));
+  return attn_launch(qr, kr, v, b, h, n, n, dh, causal, scale, dtype, out, st);
 }

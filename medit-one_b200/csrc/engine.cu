@@ -30,6 +30,7 @@
 #include "gemm.cuh"
 #include "ops.cuh"
 #include "rows.cuh"
+#include "flash_attn.cuh"
 
 using namespace one;
 
@@ -308,6 +309,7 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(row_attn_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(moe_router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(moe_router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
+  CK(cudaFuncSetAttribute(flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem));
   g_attrs_set = true;
   return ONE_OK;
 }

@@ -9,6 +9,7 @@ namespace one {
 // fp32, emb = cat(freqs, freqs), cos / sin cast to the output dtype.
 template <typename T>
 __global__ void rotary_kernel(const int64_t* pos, int n, const float* inv_freq, int dim, T* cos_out, T* sin_out) {
+  pdl_wait();  // launched with programmatic stream serialization: inputs visible after this
   const int half = dim / 2;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)n * half) return;
@@ -25,6 +26,7 @@ __global__ void rotary_kernel(const int64_t* pos, int n, const float* inv_freq, 
 // divided by (s + 1 + 1e-8) in fp32, cast back. One thread per (batch, feature).
 template <typename T>
 __global__ void cumsum_norm_kernel(const T* x, int b, int s, int d, int seq_len, T* out) {
+  pdl_wait();  // launched with programmatic stream serialization: inputs visible after this
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)b * d) return;
   const int bb = (int)(idx / d), j = (int)(idx % d);
@@ -43,6 +45,7 @@ template <typename T>
 __global__ void combined_rope_attn_kernel(const T* sx, const T* ky, const T* va, const T* cosv, const T* sinv, int cos_b,
                                           const T* wq, const T* bq, const T* wk, const T* bk, const T* wv, const T* bv,
                                           int b, int h, int t, int dh, int hout, T* out) {
+  pdl_wait();  // launched with programmatic stream serialization: inputs visible after this
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)b * h * t) return;
   const int ti = (int)(idx % t);
@@ -102,6 +105,7 @@ __global__ void combined_rope_attn_kernel(const T* sx, const T* ky, const T* va,
 template <typename T>
 __global__ void __launch_bounds__(64) attn_simt_kernel(const T* q, const T* k, const T* v, int nq, int nk, int dh,
                                                        int causal, float scale, T* out) {
+  pdl_wait();  // launched with programmatic stream serialization: inputs visible after this
   __shared__ float sK[64][65];
   __shared__ float sV[64][65];
   const int bh = blockIdx.y;

@@ -64,6 +64,11 @@ SIGNATURES = {
                                             c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "one_flash_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
                                     c_float, c_int32, c_void_p, c_void_p]),
+    "one_rope_flash_attention_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "one_rope_flash_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                         c_int32, c_int32, c_int32, c_float, c_int32, c_void_p, c_void_p, c_size_t,
+                                         c_void_p]),
+    "one_ops_error": (c_int, [POINTER(c_int32), c_int32]),
 }
 
 

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import torch
 
-from .turbo_ops import turbo_flash_attention
+from .turbo_ops import turbo_flash_attention, turbo_rope_flash_attention
 
 
 def rotate_half(x):
@@ -30,6 +30,14 @@ def flash_attention(q, k, v, dropout_p=0.0, causal=False):
     if dropout_p:
         raise NotImplementedError("the inference engine has no dropout")
     return turbo_flash_attention(q, k, v, causal=causal)
+
+
+def rope_flash_attention(q, k, v, cos, sin, dropout_p=0.0, causal=False):
+    """apply_rotary_pos_emb_flash(q, k, cos, sin) then flash_attention(q, k, v) in one fused
+    native call: the isolated RoPE + attention workload. cos, sin [B or 1, N, Dh]."""
+    if dropout_p:
+        raise NotImplementedError("the inference engine has no dropout")
+    return turbo_rope_flash_attention(q, k, v, cos, sin, causal=causal)
 
 
 class OneFlashAttention(torch.nn.Module):

@@ -48,6 +48,42 @@ def turbo_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cau
     return out
 
 
+def turbo_rope_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor,
+                               sin: torch.Tensor, causal: bool = True,
+                               scale_factor: Optional[float] = None) -> torch.Tensor:
+    """apply_rotary_pos_emb_flash(q, k, cos, sin) (one/flash_attention.py:26-33) followed by
+    turbo_flash_attention, as one native call. q, k, v [B, H, N, Dh]; cos, sin [B or 1, N, Dh]
+    in q's dtype (OneRotaryEmbedding's output)."""
+    _need(q, k, v, cos, sin)
+    if scale_factor is None:
+        scale_factor = 1.0 / (q.size(-1) ** 0.5)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    cos, sin = cos.to(q.dtype).contiguous(), sin.to(q.dtype).contiguous()
+    B, H, N, Dh = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k and v must have the same shape [B, H, N, Dh]")
+    cb = cos.shape[0] if cos.dim() == 3 else 1
+    if cos.shape[-2:] != (N, Dh) or sin.shape != cos.shape or cb not in (1, B):
+        raise ValueError(f"cos / sin must be [B or 1, {N}, {Dh}], got {tuple(cos.shape)}")
+    dt = C.dtype_code(q.dtype)
+    ws = torch.empty(C.LIB.one_rope_flash_attention_workspace_bytes(B, H, N, Dh, dt), dtype=torch.uint8,
+                     device=q.device)
+    out = torch.empty_like(q)
+    C.check(C.LIB.one_rope_flash_attention(C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(cos), C.ptr(sin), cb, B, H, N, Dh,
+                                           1 if causal else 0, float(scale_factor), dt, C.ptr(out), C.ptr(ws),
+                                           ws.numel(), _stream()),
+            "one_rope_flash_attention")
+    return out
+
+
+def ops_error(clear: bool = True) -> Tuple[int, int]:
+    """(code, site) of the standalone ops' device error record (0 = none); synchronises."""
+    _need()
+    where = ctypes.c_int32(0)
+    code = C.LIB.one_ops_error(ctypes.byref(where), 1 if clear else 0)
+    return int(code), int(where.value)
+
+
 def turbo_moe_routing(inputs: torch.Tensor, experts_weights: torch.Tensor, top_k: int) -> torch.Tensor:
     """The reference's turbo_moe_routing (one/turbo_ops.py:146-172) returns its inputs: its
     PyTorch path computes a top-k that it discards. Kept as is. The LinearMoE router itself

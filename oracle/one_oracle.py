@@ -321,6 +321,15 @@ def exact_attention(q: Tensor, k: Tensor, v: Tensor, causal: bool, scale: Option
     return torch.matmul(w, v)
 
 
+def rope_exact_attention(q: Tensor, k: Tensor, v: Tensor, cos: Tensor, sin: Tensor, causal: bool,
+                         scale: Optional[float] = None) -> Tensor:
+    """The isolated RoPE + attention workload: apply_rotary_pos_emb_flash
+    (one/flash_attention.py:26-33) on q and k, then turbo_flash_attention's exact PyTorch
+    path (one/turbo_ops.py:115-143)."""
+    qr, kr = apply_rope(q, k, cos, sin)
+    return exact_attention(qr, kr, v, causal, scale)
+
+
 def exact_attention_fp32(q: Tensor, k: Tensor, v: Tensor, causal: bool, scale: Optional[float] = None) -> Tensor:
     """flash_attention()'s fp32 fallback (one/flash_attention.py:242-282): the whole
     attention in fp32, cast back to the input dtype at the end."""

@@ -180,6 +180,23 @@ def gen_attention():
                 out[f"turbo_{tag}"] = f32(turbo_ops.turbo_flash_attention(qq, kk, vv, causal=causal))
                 out[f"flash_{tag}"] = f32(flash_attention.FlashAttentionFunction.apply(qq, kk, vv, 0.0, causal))
         out[f"q_n{N}"], out[f"k_n{N}"], out[f"v_n{N}"] = f32(q), f32(k), f32(v)
+    # RoPE + attention across several 128-key tiles with a ragged end: the reference's
+    # rotary embedding (turbo_rotary_embedding_cpu), apply_rotary_pos_emb_flash and the exact
+    # PyTorch path of turbo_flash_attention, in that order.
+    g = torch.Generator().manual_seed(21)
+    inv = _default_rope(configuration_one.OneConfig(**TINY))[0]
+    for N, dts in ((200, ("fp32", "bf16")), (300, ("bf16",))):
+        q, k, v = (torch.randn(1, 2, N, 64, generator=g) for _ in range(3))
+        pos = torch.arange(0, N).unsqueeze(0)
+        for name in dts:
+            dt = torch.float32 if name == "fp32" else torch.bfloat16
+            qq, kk, vv = q.to(dt), k.to(dt), v.to(dt)
+            c, s = turbo_ops.turbo_rotary_embedding_cpu(qq, pos, inv)
+            qr, kr = flash_attention.apply_rotary_pos_emb_flash(qq, kk, c, s)
+            for causal in (False, True):
+                tag = f"n{N}_{name}_{'c' if causal else 'nc'}"
+                out[f"rope_{tag}"] = f32(turbo_ops.turbo_flash_attention(qr, kr, vv, causal=causal))
+        out[f"rq_n{N}"], out[f"rk_n{N}"], out[f"rv_n{N}"] = f32(q), f32(k), f32(v)
     np.savez_compressed(os.path.join(HERE, "attention.npz"), **out)
     print("attention", len(out))
 

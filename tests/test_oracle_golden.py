@@ -127,6 +127,16 @@ def test_attention_matches_reference(n, dt, causal):
     np.testing.assert_array_equal(O.blockwise_flash_attention(q, k, v, causal).float().numpy(), g[f"flash_{tag}"])
 
 
+@pytest.mark.parametrize("n,dt", [(200, "fp32"), (200, "bf16"), (300, "bf16")])
+@pytest.mark.parametrize("causal", [False, True])
+def test_rope_attention_matches_reference(n, dt, causal):
+    g = load("attention.npz")
+    q, k, v = (torch.from_numpy(g[f"r{c}_n{n}"]).to(DT[dt]) for c in "qkv")
+    cos, sin = O.rope_cos_sin(O.rope_inv_freq(64, 10000.0), torch.arange(0, n).unsqueeze(0), DT[dt])
+    tag = f"n{n}_{dt}_{'c' if causal else 'nc'}"
+    np.testing.assert_array_equal(O.rope_exact_attention(q, k, v, cos, sin, causal).float().numpy(), g[f"rope_{tag}"])
+
+
 @pytest.mark.parametrize("dt", ["fp32", "bf16"])
 def test_ops_match_reference(dt):
     g = load("ops.npz")
