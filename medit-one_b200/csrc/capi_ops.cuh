@@ -210,11 +210,19 @@ static int attn_launch(const void* q, const void* k, const void* v, int b, int h
     p.causal = causal ? 1 : 0;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.err = ops_err_ptr();
-    static int resident = -1;
+    static int resident = -1, regs = -1;
     if (resident < 0) {
+      cudaFuncAttributes fa;
+      CK(cudaFuncGetAttributes(&fa, flash_attn_tc_kernel));
+      regs = fa.numRegs;
       CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, flash_attn_tc_kernel, kFaThreads, kFaSmem));
     }
     if (resident < 1) return fail(ONE_ERR_CUDA, "attention kernel does not fit on an SM (registers / shared memory)");
+    // the kernel's setmaxnreg split assumes exactly this launch allocation; with fewer
+    // registers the softmax warpgroups' increase could not be met
+    if (regs != kFaRegsLaunch)
+      return fail(ONE_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, expected %d", regs,
+                  kFaRegsLaunch);
     const int pairs = (nq + kFaRows * kFaQTiles - 1) / (kFaRows * kFaQTiles);
     if (pairs > 65535) return fail(ONE_ERR_UNSUPPORTED, "attention: nq too large");
     e = launch_k(flash_attn_tc_kernel, dim3(bh, pairs), dim3(kFaThreads), kFaSmem, st, p);

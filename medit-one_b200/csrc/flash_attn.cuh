@@ -7,17 +7,21 @@
 // top-left aligned (torch.triu(..., diagonal=1)): query i sees keys 0..i.
 //
 // One CTA takes two 128-row query tiles of one (batch, head) and streams the head's keys
-// in 128-key tiles:
-//   warp 0      TMA producer: Q tiles once, then K and V tiles through a 3-stage ring
-//   warp 1      allocates TMEM; one thread issues tcgen05.mma:
-//                 S_t = Q_t K_j^T   (M 128, N 128, K 64; both operands K-major in smem)
-//                 O_t += P_t V_j    (M 128, N 64, K 128; P K-major, V MN-major)
-//   warps 2-9   two softmax warpgroups, one per query tile, one thread per query row:
-//                 S row from TMEM -> running max -> p = 2^(s*scale*log2e - m) -> P row
-//                 (bf16, 128-byte swizzle) in smem for the P V MMA; row sums in fp32
-// TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,320), O_1 [320,384) of a 512-column
-// allocation. While one warpgroup exponentiates, the tensor core runs the other tile's
-// S and the P V products, so the two tiles ping-pong.
+// in 128-key tiles. Twelve warps in three warpgroups:
+//   warps 0-3, 4-7   softmax warpgroups, one per query tile, one thread per query row:
+//                      S row from TMEM (128 fp32 registers) -> running max ->
+//                      p = 2^(s*scale*log2e - m) -> bf16 P row back into TMEM
+//   warp 8           TMA producer: Q tiles once, then K and V tiles through a 3-stage ring
+//   warp 9           allocates TMEM; one thread issues tcgen05.mma:
+//                      S_t = Q_t K_j^T   (M 128, N 128, K 64; both operands K-major in smem)
+//                      O_t += P_t V_j    (M 128, N 64, K 128; P read from TMEM, V MN-major)
+//   warps 10-11      idle
+// The third warpgroup gives up registers (setmaxnreg) so the softmax threads can hold a
+// whole score row: 168 per thread at launch, 208 for softmax, 88 for the rest.
+// TMEM columns (512): S_0 [0,128), S_1 [128,256), O_0 [256,320), O_1 [320,384),
+// P_0 [384,448), P_1 [448,512) (bf16 pairs, one 32-bit column per two keys). A softmax thread releases S_t as soon as the row is in registers, so the
+// MMA thread computes S_t for key tile j + 1 while softmax t works on tile j; the two
+// query tiles interleave on the tensor core.
 //
 // The running max is rescaled lazily: O and the row sum are multiplied by 2^(m_old-m_new)
 // only when the max has grown by more than 2^8; otherwise p keeps the older, smaller
@@ -36,14 +40,23 @@ constexpr int kFaKeys = 128;   // keys per K / V tile
 constexpr int kFaDh = 64;      // head dim handled by the tensor-core kernel
 constexpr int kFaQTiles = 2;   // query tiles per CTA
 constexpr int kFaStages = 3;   // K / V ring depth
-constexpr int kFaThreads = 64 + 128 * kFaQTiles;
+constexpr int kFaThreads = 128 * (kFaQTiles + 1);
+constexpr int kFaProducerWarp = 4 * kFaQTiles;
+constexpr int kFaMmaWarp = kFaProducerWarp + 1;
+// Registers: 65536 per SM in four sub-partitions of 16384; 12 warps -> 3 per sub-partition
+// -> 168 per thread at launch. setmaxnreg moves 80 per thread from the third warpgroup to
+// the two softmax warpgroups (40 each); the MMA and TMA code needs 88 without spilling.
+constexpr int kFaRegsLaunch = 168;
+constexpr int kFaRegsSoftmax = 208;
+constexpr int kFaRegsOther = 88;
+static_assert(kFaQTiles * 128 * kFaRegsSoftmax + 128 * kFaRegsOther <= kFaThreads * kFaRegsLaunch,
+              "register split exceeds the launch allocation");
 constexpr uint32_t kFaTile = kFaRows * kFaDh * 2;     // one Q, K or V tile: 16 KB
-constexpr uint32_t kFaPTile = kFaRows * kFaKeys * 2;  // one P tile: 32 KB (two 64-key halves)
+constexpr uint32_t kFaTmemCols = 512;
 constexpr uint32_t kFaOffQ = 0;
 constexpr uint32_t kFaOffK = kFaOffQ + kFaQTiles * kFaTile;
 constexpr uint32_t kFaOffV = kFaOffK + kFaStages * kFaTile;
-constexpr uint32_t kFaOffP = kFaOffV + kFaStages * kFaTile;
-constexpr uint32_t kFaOffBar = kFaOffP + kFaQTiles * kFaPTile;
+constexpr uint32_t kFaOffBar = kFaOffV + kFaStages * kFaTile;
 // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[Q], s_free[Q],
 // p_full[Q], o_full[Q], done
 constexpr int kFaBarQ = 0;
@@ -58,9 +71,10 @@ constexpr int kFaBarOF = kFaBarPF + kFaQTiles;
 constexpr int kFaBarDone = kFaBarOF + kFaQTiles;
 constexpr int kFaBars = kFaBarDone + 1;
 constexpr size_t kFaSmem = kFaOffBar + kFaBars * 8 + 16 + 1024;  // + TMEM slot + 1 KB alignment slack
-constexpr uint32_t kFaTmemCols = 512;
 static_assert(kFaSmem <= 227 * 1024, "attention tile ring exceeds shared memory");
-static_assert(kFaOffK % 1024 == 0 && kFaOffV % 1024 == 0 && kFaOffP % 1024 == 0, "swizzled tiles need 1 KB alignment");
+static_assert(kFaOffK % 1024 == 0 && kFaOffV % 1024 == 0, "swizzled tiles need 1 KB alignment");
+constexpr uint32_t kFaColS = 0, kFaColO = kFaQTiles * kFaKeys, kFaColP = kFaColO + kFaQTiles * kFaDh;
+static_assert(kFaColP + kFaQTiles * kFaKeys / 2 <= kFaTmemCols, "TMEM columns");
 
 struct FaParams {
   CUtensorMap tq, tk, tv;  // [bh][n][64] bf16, box {64, 128, 1}, 128-byte swizzle, zero fill
@@ -78,8 +92,11 @@ ONE_DEVINL int fa_key_tiles(int q_row0, int nq, int nk, int causal) {
   return n;
 }
 
-// Registers are allocated per SM sub-partition (16384 each): ten warps put three on two of
-// them, so the bound is 168 registers per thread.
+template <int N>
+ONE_DEVINL void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+ONE_DEVINL void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+
 __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __grid_constant__ FaParams p) {
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -115,7 +132,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
     mbar_init(&bar[kFaBarDone], 1);
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kFaMmaWarp) {
     tmem_alloc(tmem_slot, kFaTmemCols);
     tmem_relinquish();
   }
@@ -124,8 +141,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp >= kFaProducerWarp) {
+    setmaxnreg_dec<kFaRegsOther>();
+    if (warp == kFaProducerWarp && lane == 0) {
       // ------------------------------------------------------------ TMA producer
       tma_prefetch_desc(&p.tq);
       tma_prefetch_desc(&p.tk);
@@ -158,35 +176,29 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
         mbar_wait(&bar[kFaBarKF + s], ph, p.err, 5);
         mbar_wait(&bar[kFaBarVF + s], ph, p.err, 6);
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == kFaMmaWarp && lane == 0) {
       // ------------------------------------------------------------ MMA issuer
       constexpr uint32_t idesc_s = umma_idesc_bf16(kFaRows, kFaKeys);
       constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(kFaRows, kFaDh);
-      bool ok = mbar_wait(&bar[kFaBarQ], 0, p.err, 7);
-      tc_fence_after();
-      // S_t = Q_t K_j^T (4 MMAs of K 16) and O_t += P_t V_j (8 MMAs of K 16; P halves 16 KB
-      // apart, 32 B per 16 keys inside a half; V advances 2 KB per 16 keys)
+      // S_t = Q_t K_j^T (4 MMAs of K 16) and O_t += P_t V_j (8 MMAs of K 16; P advances 8
+      // TMEM columns and V 2 KB per 16 keys)
       auto issue_s = [&](int t, int s) {
         const uint64_t a = umma_desc_sw128(sm + kFaOffQ + t * kFaTile);
         const uint64_t b = umma_desc_sw128(sm + kFaOffK + s * kFaTile);
 #pragma unroll
         for (int kk = 0; kk < kFaDh / 16; ++kk)
-          umma_bf16(tmem + t * kFaKeys, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16(tmem + kFaColS + t * kFaKeys, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(&bar[kFaBarSF + t]);
       };
       auto issue_pv = [&](int t, int s, bool acc) {
-        const uint64_t a = umma_desc_sw128(sm + kFaOffP + t * kFaPTile);
         const uint64_t b = umma_desc_sw128_mn(sm + kFaOffV + s * kFaTile, kFaTile);
 #pragma unroll
-        for (int kk = 0; kk < kFaKeys / 16; ++kk) {
-          const uint64_t ak = a + (uint64_t)((kk >> 2) * (16384 >> 4) + (kk & 3) * 2);
-          const uint64_t bk = b + (uint64_t)(kk * (2048 >> 4));
-          umma_bf16(tmem + 2 * kFaKeys + t * kFaDh, ak, bk, idesc_o, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kFaKeys / 16; ++kk)
+          umma_bf16_ta(tmem + kFaColO + t * kFaDh, tmem + kFaColP + t * (kFaKeys / 2) + kk * 8,
+                       b + (uint64_t)(kk * (2048 >> 4)), idesc_o, (acc || kk > 0) ? 1u : 0u);
         umma_commit(&bar[kFaBarOF + t]);
       };
+      bool ok = mbar_wait(&bar[kFaBarQ], 0, p.err, 7);
       if (ok && nkt_max > 0 && (ok = mbar_wait(&bar[kFaBarKF], 0, p.err, 8))) {
         tc_fence_after();
 #pragma unroll
@@ -194,32 +206,32 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
           if (nkt[t] > 0) issue_s(t, 0);
         umma_commit(&bar[kFaBarKE]);
       }
-      // per key tile j, tile by tile: P_t V_j as soon as softmax t has written P_t, then
-      // S_t for key tile j + 1 into the buffer softmax t has just read
+      // per key tile j: S_t for tile j + 1 as soon as softmax t holds S_t(j) in registers,
+      // then O_t += P_t V_j as soon as softmax t has written P_t(j)
       for (int j = 0; ok && j < nkt_max; ++j) {
         const int s = j % kFaStages, s1 = (j + 1) % kFaStages;
-        bool k_ready = false;
-        if (!(ok = mbar_wait(&bar[kFaBarVF + s], (j / kFaStages) & 1, p.err, 9))) break;
+        if (j + 1 < nkt_max) {
+          if (!(ok = mbar_wait(&bar[kFaBarKF + s1], ((j + 1) / kFaStages) & 1, p.err, 9))) break;
 #pragma unroll
-        for (int t = 0; t < kFaQTiles; ++t) {
-          if (j < nkt[t]) {
-            if (!(ok = mbar_wait(&bar[kFaBarPF + t], j & 1, p.err, 10))) break;
-            tc_fence_after();
-            issue_pv(t, s, j > 0);
-          }
-          if (j + 1 < nkt[t]) {
-            if (!k_ready) {
-              if (!(ok = mbar_wait(&bar[kFaBarKF + s1], ((j + 1) / kFaStages) & 1, p.err, 11))) break;
-              k_ready = true;
-            }
-            if (!(ok = mbar_wait(&bar[kFaBarSE + t], j & 1, p.err, 12))) break;
+          for (int t = 0; t < kFaQTiles; ++t) {
+            if (j + 1 >= nkt[t]) continue;
+            if (!(ok = mbar_wait(&bar[kFaBarSE + t], j & 1, p.err, 10))) break;
             tc_fence_after();
             issue_s(t, s1);
           }
+          if (!ok) break;
+          umma_commit(&bar[kFaBarKE + s1]);
+        }
+        if (!(ok = mbar_wait(&bar[kFaBarVF + s], (j / kFaStages) & 1, p.err, 11))) break;
+#pragma unroll
+        for (int t = 0; t < kFaQTiles; ++t) {
+          if (j >= nkt[t]) continue;
+          if (!(ok = mbar_wait(&bar[kFaBarPF + t], j & 1, p.err, 12))) break;
+          tc_fence_after();
+          issue_pv(t, s, j > 0);
         }
         if (!ok) break;
         umma_commit(&bar[kFaBarVE + s]);
-        if (k_ready) umma_commit(&bar[kFaBarKE + s1]);
       }
       // every MMA issued above completes before TMEM is freed
       umma_commit(&bar[kFaBarDone]);
@@ -227,15 +239,15 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
     }
   } else {
     // -------------------------------------------------------------- softmax warpgroups
-    const int t = (warp - 2) >> 2;
+    setmaxnreg_inc<kFaRegsSoftmax>();
+    const int t = warp >> 2;
     const int lg = warp & 3;  // TMEM lane quarter this warp may access
     const int r = lg * 32 + lane;
     const int row = q0 + t * kFaRows + r;
     const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
-    const uint32_t tS = tmem + lane_off + t * kFaKeys;
-    const uint32_t tO = tmem + lane_off + 2 * kFaKeys + t * kFaDh;
-    uint8_t* prow = sm + kFaOffP + t * kFaPTile + r * 128;
-    const int swz = r & 7;
+    const uint32_t tS = tmem + lane_off + kFaColS + t * kFaKeys;
+    const uint32_t tO = tmem + lane_off + kFaColO + t * kFaDh;
+    const uint32_t tP = tmem + lane_off + kFaColP + t * (kFaKeys / 2);
     const float sl2 = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -247,34 +259,31 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
       ok = __all_sync(0xffffffffu, mbar_wait(&bar[kFaBarSF + t], j & 1, p.err, 14));
       if (!ok) break;
       tc_fence_after();
-      // scores rounded to bf16 as the reference's bf16 matmul rounds them, kept as packed
-      // pairs; masked keys become -inf
-      const int key0 = j * kFaKeys;
-      const bool masked = key0 + kFaKeys > p.nk || (p.causal && key0 + kFaKeys - 1 > q0 + t * kFaRows);
-      const int lim = p.causal ? min(p.nk, row + 1) : p.nk;  // keys < lim are visible
-      uint32_t sp[kFaKeys / 2];
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      float s[kFaKeys];
 #pragma unroll
-      for (int h = 0; h < kFaKeys; h += 32) {
-        float v[32];
-        tmem_ld32(tS + h, v);
-        tmem_ld_wait();
-        if (masked) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (key0 + h + c >= lim) v[c] = -INFINITY;
-        }
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          mx0 = fmaxf(mx0, v[c]);
-          mx1 = fmaxf(mx1, v[c + 1]);
-          sp[(h + c) / 2] = pack_bf16x2(v[c], v[c + 1]);
-        }
-      }
+      for (int c = 0; c < kFaKeys; c += 32) tmem_ld32(tS + c, s + c);
+      tmem_ld_wait();
+      // S_t is in registers: the MMA thread may overwrite it with the next key tile
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kFaBarSE + t]);
-      const float m_new = fmaxf(m_used, rnd<__nv_bfloat16>(fmaxf(mx0, mx1)) * sl2);
+      const int key0 = j * kFaKeys;
+      if (key0 + kFaKeys > p.nk || (p.causal && key0 + kFaKeys - 1 > q0 + t * kFaRows)) {
+        const int lim = p.causal ? min(p.nk, row + 1) : p.nk;  // keys < lim are visible
+#pragma unroll
+        for (int c = 0; c < kFaKeys; ++c)
+          if (key0 + c >= lim) s[c] = -INFINITY;
+      }
+      // row max: four independent chains of three-input max
+      float mx[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        mx[c] = s[32 * c];
+#pragma unroll
+        for (int i = 1; i < 31; i += 2) mx[c] = fmax3(mx[c], s[32 * c + i], s[32 * c + i + 1]);
+        mx[c] = fmaxf(mx[c], s[32 * c + 31]);
+      }
+      const float m_new = fmaxf(m_used, fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * sl2);
       const bool need = m_new > m_used + 8.f;
       const float fac = need ? ex2_approx(m_used - m_new) : 1.f;
       if (need) {
@@ -283,7 +292,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
       }
       const float mb = m_used == -INFINITY ? 0.f : m_used;
       if (j > 0) {
-        // P V of the previous key tile has finished: the P buffer is free and O is stable
+        // P V of the previous key tile has finished: P_t is free and O_t is stable
         ok = __all_sync(0xffffffffu, mbar_wait(&bar[kFaBarOF + t], (j - 1) & 1, p.err, 15));
         if (!ok) break;
         tc_fence_after();
@@ -297,29 +306,25 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
             for (int i = 0; i < 16; ++i) o[i] *= fac;
             tmem_st16(tO + c, o);
           }
-          tmem_st_wait();
         }
       }
-      // p = 2^(s*scale*log2e - m) -> bf16 P row in shared memory, 8 keys (16 B) at a time, in
-      // the 128-byte-swizzled K-major layout the MMA reads (two 64-key halves 16 KB apart)
+      // p = 2^(s*scale*log2e - m) as bf16 pairs into P_t, 64 keys (32 columns) at a time
       float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-      for (int c8 = 0; c8 < kFaKeys / 8; ++c8) {
-        uint32_t pk[4];
+      for (int h = 0; h < kFaKeys; h += 64) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t w = sp[4 * c8 + i];
-          const float p0 = ex2_approx(fmaf(__uint_as_float(w << 16), sl2, -mb));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(w & 0xffff0000u), sl2, -mb));
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2_approx(fmaf(s[h + 2 * i], sl2, -mb));
+          const float p1 = ex2_approx(fmaf(s[h + 2 * i + 1], sl2, -mb));
           l0 += p0;
           l1 += p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(prow + (c8 >> 3) * 16384 + (((c8 & 7) ^ swz) << 4)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st32(tP + h / 2, pk);
       }
       l += l0 + l1;
-      fence_proxy_async();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kFaBarPF + t]);
@@ -346,7 +351,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kFaTmemCols);
+  if (warp == kFaMmaWarp) tmem_dealloc(tmem, kFaTmemCols);
 }
 
 // x * cos + rotate_half(x) * sin (one/flash_attention.py:20-33) on q and k rows of 64,
