@@ -1,6 +1,7 @@
 """Decode throughput of the 140M-class MedIT One model in bf16 on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+                    [--workload decode|attention]
 
 Workload (per GPU, weak scaling): 256 sequences, prompt of 128 tokens (ids uniform in
 [0, 32000), seed 4 + rank), then greedy single-token decode steps carrying the
@@ -310,6 +311,151 @@ def run_native(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+ATT_SHAPE = (8, 12, 2048, 64)
+ATT_METRIC = "fused RoPE + attention TFLOP/s (Q/K/V [8,12,2048,64] bf16, causal + non-causal)"
+
+
+def attention_flops(b, h, n, d, causal):
+    """Algorithmic FLOPs of softmax(q k^T) v: 2 matmuls of 2*n*n_keys*d per head; under the
+    causal mask each query row sees row+1 keys."""
+    keys = n * (n + 1) / 2 if causal else n * n
+    return 4.0 * b * h * d * keys
+
+
+def attention_inputs(device):
+    from one import turbo_ops
+    from one.engine import rope_inv_freq
+    B, H, N, D = ATT_SHAPE
+    g = torch.Generator().manual_seed(2)
+    q, k, v = (torch.randn(B, H, N, D, generator=g).bfloat16() for _ in range(3))
+    pos = torch.arange(0, N).unsqueeze(0)
+    if device == "cpu":
+        return q, k, v, pos
+    q, k, v = q.to(device), k.to(device), v.to(device)
+    cos, sin = turbo_ops.turbo_rotary_embedding(q, pos.to(device), rope_inv_freq(D, 10000.0).to(device))
+    return q, k, v, cos, sin
+
+
+def attention_cpu(heads: int) -> dict:
+    """The reference's RoPE + exact attention (oracle restatement) on the host CPU for a
+    bounded sample of `heads` (batch, head) pairs of the workload, causal and non-causal."""
+    from oracle import one_oracle as O
+    B, H, N, D = ATT_SHAPE
+    torch.set_num_threads(os.cpu_count() or 1)
+    q, k, v, pos = attention_inputs("cpu")
+    cos, sin = O.rope_cos_sin(O.rope_inv_freq(D, 10000.0), pos, torch.bfloat16)
+    qs, ks, vs = (x.reshape(B * H, N, D)[:heads].unsqueeze(0) for x in (q, k, v))
+    O.rope_exact_attention(qs[:, :1], ks[:, :1], vs[:, :1], cos, sin, False)  # warm-up
+    t0 = time.perf_counter()
+    for causal in (False, True):
+        for h0 in range(0, heads, 8):  # 8 heads at a time bounds the score matrices' memory
+            O.rope_exact_attention(qs[:, h0:h0 + 8], ks[:, h0:h0 + 8], vs[:, h0:h0 + 8], cos, sin, causal)
+    dt = time.perf_counter() - t0
+    fl = sum(attention_flops(1, heads, N, D, c) for c in (False, True))
+    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{heads} of {B * H} (batch, head) pairs, causal and non-causal, oracle restatement of "
+                      f"apply_rotary_pos_emb_flash + turbo_flash_attention's exact path in bf16", "seconds": dt}
+
+
+def run_attention(args, ws, rank, local):
+    """One step = the fused RoPE + attention op on the whole workload, non-causal then causal."""
+    import ctypes
+    from one import _capi as C, turbo_ops
+    B, H, N, D = ATT_SHAPE
+    dev = f"cuda:{local}"
+    q, k, v, cos, sin = attention_inputs(dev)
+    out = torch.empty_like(q)
+    ws_buf = torch.empty(C.LIB.one_rope_flash_attention_workspace_bytes(B, H, N, D, 0), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    st = ctypes.c_void_p(stream.cuda_stream)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > L2: inputs are 75 MB
+
+    def op(causal):
+        C.check(C.LIB.one_rope_flash_attention(C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(cos), C.ptr(sin), 1, B, H, N, D,
+                                               1 if causal else 0, 0.125, 0, C.ptr(out), C.ptr(ws_buf),
+                                               ws_buf.numel(), st), "one_rope_flash_attention")
+
+    for _ in range(args.warmup):
+        op(False)
+        op(True)
+    torch.cuda.synchronize()
+    barrier(ws)
+    per = {False: 0.0, True: 0.0}
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(2 * args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            for c, causal in enumerate((False, True)):
+                flush.zero_()
+                e0, e1 = ev[2 * i + c]
+                e0.record(stream)
+                op(causal)
+                e1.record(stream)
+        torch.cuda.synchronize()
+    for i in range(args.steps):
+        for c, causal in enumerate((False, True)):
+            per[causal] += ev[2 * i + c][0].elapsed_time(ev[2 * i + c][1])
+    barrier(ws)
+    ms = max_over_ranks(ws, per[False] + per[True])
+    fl_step = attention_flops(B, H, N, D, False) + attention_flops(B, H, N, D, True)
+    value = ws * fl_step * args.steps / (ms / 1000.0) / 1e12
+    if turbo_ops.ops_error() != (0, 0):
+        raise RuntimeError("device error in the attention kernels")
+
+    # e2e through the public API: host q/k/v/cos/sin in, host output back, every step
+    hq, hk, hv, hc, hs = (x.cpu().pin_memory() for x in (q, k, v, cos, sin))
+    for _ in range(2):
+        turbo_ops.turbo_rope_flash_attention(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True),
+                                             hv.to(dev, non_blocking=True), hc.to(dev, non_blocking=True),
+                                             hs.to(dev, non_blocking=True), causal=False).cpu()
+    torch.cuda.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for causal in (False, True):
+            o = turbo_ops.turbo_rope_flash_attention(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True),
+                                                     hv.to(dev, non_blocking=True), hc.to(dev, non_blocking=True),
+                                                     hs.to(dev, non_blocking=True), causal=causal)
+            o.cpu()
+    e1.record(stream)
+    e1.synchronize()
+    e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
+    e2e = ws * fl_step * args.steps / (e_ms / 1000.0) / 1e12
+    h2d = 2 * sum(x.numel() * x.element_size() for x in (hq, hk, hv, hc, hs))
+    d2h = 2 * out.numel() * out.element_size()
+
+    _, tf, _, src = peaks()
+    clocks = clk.summary()
+    if rank == 0:
+        line = {"metric": ATT_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (Q/K/V ~ N(0,1) seed 2, RoPE base 1e4)",
+                "config": {"workload": "isolated fused RoPE + flash attention, Q/K/V [8, 12, 2048, 64] bf16, "
+                                       "scale 1/8, one non-causal and one causal call per step",
+                           "us_noncausal": 1000 * per[False] / args.steps, "us_causal": 1000 * per[True] / args.steps,
+                           "l2": "256 MB buffer written between timed calls (inputs 75 MB < L2)"},
+                "roofline": {"bound": "tensor", "kernel": "flash_attn_tc_kernel + rope_qk_kernel",
+                             "achieved": value / ws, "peak": tf, "unit": "TFLOP/s", "frac": value / ws / tf,
+                             "peak_source": src, "traffic": None},
+                "e2e": {"value": e2e, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "gpu_launches": 4 * args.steps, "clocks": clocks}
+        if ws == 1 and not args.no_cpu_baseline:
+            r = attention_cpu(96)
+            line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+
+
+def run_attention_reference(args):
+    r = attention_cpu(96)
+    line = {"impl": "reference", "metric": ATT_METRIC, "value": r["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": 1, "warmup": 1, "ms_per_step": 1000 * r["seconds"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (Q/K/V ~ N(0,1) seed 2, RoPE base 1e4)",
+            "config": {"workload": "isolated fused RoPE + flash attention, Q/K/V [8, 12, 2048, 64] bf16"},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def profile_case(args):
     """Small fixed case for ncu captures: 140M engine at batch 256, a 16-token prompt, then
     three graph-replayed decode steps (launch order: prompt kernels, then 76 per step)."""
@@ -338,6 +484,8 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
+    ap.add_argument("--workload", default="decode", choices=["decode", "attention"],
+                    help="decode: the 140M decode step (default); attention: the isolated RoPE + attention op")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
@@ -345,11 +493,17 @@ def main():
     if args.impl == "reference":
         # rank 0 alone times the host-CPU reference; other ranks exit without work
         if int(os.environ.get("RANK", "0")) == 0:
-            run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), 0)
+            if args.workload == "attention":
+                run_attention_reference(args)
+            else:
+                run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), 0)
         return
     ws, rank, local = dist_init()
     try:
-        run_native(args, ws, rank, local)
+        if args.workload == "attention":
+            run_attention(args, ws, rank, local)
+        else:
+            run_native(args, ws, rank, local)
     finally:
         if ws > 1:
             import torch.distributed as dist
