@@ -274,6 +274,28 @@ ONE_DEVINL float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed fp32 pair arithmetic (fma.rn.f32x2 / add.rn.f32x2, sm_100): one instruction for
+// two lanes' worth of independent fp32 work.
+ONE_DEVINL uint64_t f2_bits(float2 a) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+  return r;
+}
+ONE_DEVINL float2 f2_from(uint64_t r) {
+  float2 a;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(r));
+  return a;
+}
+ONE_DEVINL float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_from(d);
+}
+ONE_DEVINL float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(d);
+}
 // max(a, b, c) in one instruction (three-input max.f32, sm_100).
 ONE_DEVINL float fmax3(float a, float b, float c) {
   float d;

@@ -308,22 +308,24 @@ __global__ void __launch_bounds__(kFaThreads, 1) flash_attn_tc_kernel(const __gr
           }
         }
       }
-      // p = 2^(s*scale*log2e - m) as bf16 pairs into P_t, 64 keys (32 columns) at a time
-      float l0 = 0.f, l1 = 0.f;
+      // p = 2^(s*scale*log2e - m) as bf16 pairs into P_t, 64 keys (32 columns) at a time;
+      // scale-subtract and row sums on packed fp32 pairs, four partial sums
+      const float2 sl2v = make_float2(sl2, sl2), nmb = make_float2(-mb, -mb);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int h = 0; h < kFaKeys; h += 64) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2_approx(fmaf(s[h + 2 * i], sl2, -mb));
-          const float p1 = ex2_approx(fmaf(s[h + 2 * i + 1], sl2, -mb));
-          l0 += p0;
-          l1 += p1;
-          pk[i] = pack_bf16x2(p0, p1);
+          const float2 x = fma2(make_float2(s[h + 2 * i], s[h + 2 * i + 1]), sl2v, nmb);
+          const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          acc[i & 3] = add2(acc[i & 3], e);
+          pk[i] = pack_bf16x2(e.x, e.y);
         }
         tmem_st32(tP + h / 2, pk);
       }
-      l += l0 + l1;
+      const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
+      l += (a01.x + a23.x) + (a01.y + a23.y);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
