@@ -1,7 +1,7 @@
 """Decode throughput of the 140M-class MedIT One model in bf16 on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
-                    [--workload decode|attention]
+                    [--workload decode|attention|linear_moe]
 
 Workload (per GPU, weak scaling): 256 sequences, prompt of 128 tokens (ids uniform in
 [0, 32000), seed 4 + rank), then greedy single-token decode steps carrying the
@@ -456,6 +456,130 @@ def run_attention_reference(args):
     print(json.dumps(line), flush=True)
 
 
+MOE_T, MOE_D, MOE_E, MOE_K, MOE_R = 16384, 768, 8, 2, 64
+MOE_METRIC = "LinearMoE TFLOP/s (16384 x 768 bf16, 8 experts top-2, r 64, 768 -> 768)"
+
+
+def moe_inputs():
+    """x ~ N(0, 1) seed 3; LinearMoE(768, 768, 8 experts, top-2, r 64) with the random-init rule
+    (weights, gate and experts N(0, 0.02), biases and bias2 zero)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(MOE_T, MOE_D, generator=g).bfloat16()
+    n = lambda *shape: torch.empty(shape).normal_(0.0, 0.02, generator=g).bfloat16()
+    p = {"weight": n(MOE_D, MOE_D), "bias": torch.zeros(MOE_D).bfloat16(), "gate": n(MOE_R, MOE_D),
+         "experts": n(MOE_E), "bias2": torch.zeros(MOE_E, MOE_D).bfloat16()}
+    return x, p
+
+
+def moe_flops(tokens):
+    """gate (D -> r) and shared Linear (D -> D) GEMMs: 2 * tokens * D * (D + r)."""
+    return 2.0 * tokens * MOE_D * (MOE_D + MOE_R)
+
+
+def moe_cpu(tokens: int) -> dict:
+    from oracle import one_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, p = moe_inputs()
+    xs = x[:tokens]
+    O.linear_moe(xs[:64], p, MOE_K)  # warm-up
+    t0 = time.perf_counter()
+    O.linear_moe(xs, p, MOE_K)
+    dt = time.perf_counter() - t0
+    return {"value": moe_flops(tokens) / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": dt,
+            "sample": f"{tokens} of {MOE_T} tokens, oracle restatement of LinearMoE.forward in bf16"}
+
+
+def run_linear_moe(args, ws, rank, local):
+    """One step = the LinearMoE operator (clamp, gate GEMM, router: softmax, expert factors,
+    exact expert sums, top-k, combine; shared Linear) on all 16384 tokens."""
+    import ctypes
+    from one import _capi as C, turbo_ops
+    dev = f"cuda:{local}"
+    x, p = moe_inputs()
+    x = x.to(dev)
+    pc = {k: v.to(dev).contiguous() for k, v in p.items()}
+    out = torch.empty(MOE_T, MOE_D, dtype=torch.bfloat16, device=dev)
+    idx = torch.empty(MOE_T, MOE_K, dtype=torch.int32, device=dev)
+    wsb = C.LIB.one_linear_moe_workspace_bytes(MOE_T, MOE_D, MOE_R, 0)
+    wsp = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    st = ctypes.c_void_p(stream.cuda_stream)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # x + out = 50 MB < L2
+
+    def op(xin, o):
+        C.check(C.LIB.one_linear_moe(C.ptr(xin), MOE_T, MOE_D, MOE_D, C.ptr(pc["weight"]), C.ptr(pc["bias"]),
+                                     C.ptr(pc["gate"]), C.ptr(pc["experts"]), C.ptr(pc["bias2"]), MOE_E, MOE_R, MOE_K,
+                                     0, C.ptr(o), C.ptr(idx), C.ptr(wsp), wsb, st), "one_linear_moe")
+
+    for _ in range(args.warmup):
+        op(x, out)
+    torch.cuda.synchronize()
+    barrier(ws)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            op(x, out)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(ws, sum(a.elapsed_time(b) for a, b in ev))
+    value = ws * moe_flops(MOE_T) * args.steps / (ms / 1000.0) / 1e12
+    code = turbo_ops.ops_error()
+    if code != (0, 0):
+        raise RuntimeError(f"device error {code}")
+    # e2e through the C ABI with host buffers: x in, y and the top-k indices out, every step
+    hx = x.cpu().pin_memory()
+    hy = torch.empty(MOE_T, MOE_D, dtype=torch.bfloat16).pin_memory()
+    hi = torch.empty(MOE_T, MOE_K, dtype=torch.int32).pin_memory()
+    xd = torch.empty_like(x)
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        xd.copy_(hx, non_blocking=True)
+        op(xd, out)
+        hy.copy_(out, non_blocking=True)
+        hi.copy_(idx, non_blocking=True)
+    e1.record(stream)
+    e1.synchronize()
+    e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
+    e2e = ws * moe_flops(MOE_T) * args.steps / (e_ms / 1000.0) / 1e12
+    _, tf, _, src = peaks()
+    clocks = clk.summary()
+    if rank == 0:
+        line = {"metric": MOE_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (x ~ N(0,1) seed 3; weights, gate, experts N(0,0.02); biases zero)",
+                "config": {"workload": "isolated LinearMoE(768, 768, num_experts=8, top_k=2, r=64) on 16384 tokens",
+                           "tokens_per_s": ws * MOE_T * args.steps / (ms / 1000.0),
+                           "l2": "256 MB buffer written between timed calls (x + y = 50 MB < L2)"},
+                "roofline": {"bound": "tensor", "kernel": "one_linear_moe (clamp, gate GEMM, router, shared GEMM)",
+                             "achieved": value / ws, "peak": tf, "unit": "TFLOP/s", "frac": value / ws / tf,
+                             "peak_source": src, "traffic": None,
+                             "algorithmic_bytes": 2 * MOE_T * MOE_D * 2 + (MOE_D + MOE_R) * MOE_D * 2},
+                "e2e": {"value": e2e, "unit": "TFLOP/s", "h2d_bytes_per_step": MOE_T * MOE_D * 2,
+                        "d2h_bytes_per_step": MOE_T * (MOE_D * 2 + MOE_K * 4)},
+                "gpu_launches": 4 * args.steps, "clocks": clocks}
+        if ws == 1 and not args.no_cpu_baseline:
+            r = moe_cpu(MOE_T)
+            line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+
+
+def run_linear_moe_reference(args):
+    r = moe_cpu(MOE_T)
+    line = {"impl": "reference", "metric": MOE_METRIC, "value": r["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": 1, "warmup": 1, "ms_per_step": 1000 * r["seconds"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (x ~ N(0,1) seed 3)",
+            "config": {"workload": "isolated LinearMoE(768, 768, num_experts=8, top_k=2, r=64) on 16384 tokens"},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def profile_case(args):
     """Small fixed case for ncu captures: 140M engine at batch 256, a 16-token prompt, then
     three graph-replayed decode steps (launch order: prompt kernels, then 76 per step)."""
@@ -484,8 +608,9 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attention"],
-                    help="decode: the 140M decode step (default); attention: the isolated RoPE + attention op")
+    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe"],
+                    help="decode: the 140M decode step (default); attention: the isolated RoPE + attention op; "
+                         "linear_moe: the isolated LinearMoE op on 16384 tokens")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
@@ -495,6 +620,8 @@ def main():
         if int(os.environ.get("RANK", "0")) == 0:
             if args.workload == "attention":
                 run_attention_reference(args)
+            elif args.workload == "linear_moe":
+                run_linear_moe_reference(args)
             else:
                 run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), 0)
         return
@@ -502,6 +629,8 @@ def main():
     try:
         if args.workload == "attention":
             run_attention(args, ws, rank, local)
+        elif args.workload == "linear_moe":
+            run_linear_moe(args, ws, rank, local)
         else:
             run_native(args, ws, rank, local)
     finally:

@@ -353,93 +353,6 @@ struct RowAttnParams {
   DevErr* err;
 };
 
-// One LinearMoE router for one token (one/linear_moe.py:53-90), executed by the CTA.
-// xs: router input in shared memory (fp32 values of model-dtype numbers).
-template <typename T>
-__device__ void cta_router(int r, int E, int k, const MoeRouter& R, int t, const float* xs, float* gl, float* cvals,
-                           double* red, float* score, int* sel) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const int in = R.in;
-  // gate logits (:56)
-  if (R.gate_w) {
-    const T* W = reinterpret_cast<const T*>(R.gate_w);
-    for (int j = tid; j < r; j += nt) {
-      float acc = 0.f;
-      const T* wr = W + (size_t)j * in;
-      for (int i = 0; i < in; ++i) acc = fmaf(ld<T>(wr + i), xs[i], acc);
-      gl[j] = rnd<T>(acc);
-    }
-  } else {
-    const T* G = reinterpret_cast<const T*>(R.glog) + (size_t)t * r;
-    for (int j = tid; j < r; j += nt) gl[j] = ld<T>(G + j);
-  }
-  __syncthreads();
-  // softmax over r in fp32 (:56), expert scores (:59-68): one warp per expert
-  if (tid < 32) {
-    float mx = -INFINITY;
-    for (int j = tid; j < r; j += 32) mx = fmaxf(mx, gl[j]);
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int j = tid; j < r; j += 32) sum += expf(gl[j] - mx);
-    sum = warp_sum(sum);
-    const float inv = 1.0f / sum;
-    __syncwarp();
-    for (int j = tid; j < r; j += 32) gl[j] = rnd<T>(expf(gl[j] - mx) * inv);
-  }
-  __syncthreads();
-  const T* EX = reinterpret_cast<const T*>(R.experts);
-  for (int e = tid; e < E; e += nt) {
-    const float ex = fminf(fmaxf(ld<T>(EX + e), -10.f), 10.f);
-    float s = 0.f;
-    for (int j = 0; j < r; ++j) s += rnd<T>(gl[j] * ex);   // fp32 sum in r order, then / r
-    float sc = fminf(fmaxf(rnd<T>(s / (float)r), -10.f), 10.f);
-    cvals[e] = rnd<T>(1.0f + rnd<T>(silu_f(sc)));
-  }
-  __syncthreads();
-  // per-expert sums of x * c_e + bias2[e] (:71-80): exact (fp64) sum, rounded once
-  const T* B2 = reinterpret_cast<const T*>(R.bias2);
-  for (int e0 = 0; e0 < E; e0 += 8) {
-    double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int i = tid; i < in; i += nt) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (e0 + e < E) acc[e] += (double)rnd<T>(rnd<T>(xs[i] * cvals[e0 + e]) + ld<T>(B2 + (size_t)(e0 + e) * in + i));
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
-    const int w = tid >> 5, lane = tid & 31;
-    if (lane == 0)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) red[w * 8 + e] = acc[e];
-    __syncthreads();
-    if (tid < 8 && e0 + tid < E) {
-      double s = 0.0;
-      for (int ww = 0; ww < (nt >> 5); ++ww) s += red[ww * 8 + tid];
-      score[e0 + tid] = rnd<T>(__double2float_rn(s));
-    }
-    __syncthreads();
-  }
-  if (tid == 0) {
-    const int kk = min(k, E);
-    topk_select(score, E, kk, sel);
-    if (R.idx_out)
-      for (int j = 0; j < kk; ++j) R.idx_out[(size_t)t * kk + j] = sel[j];
-  }
-  __syncthreads();
-  // mean of the selected biased inputs (:87-90), fp32 sum in selection order
-  const int kk = min(k, E);
-  T* C = reinterpret_cast<T*>(R.comb) + (size_t)t * in;
-  for (int i = tid; i < in; i += nt) {
-    float s = 0.f;
-    for (int j = 0; j < kk; ++j) {
-      const int e = sel[j];
-      s += rnd<T>(rnd<T>(xs[i] * cvals[e]) + ld<T>(B2 + (size_t)e * in + i));
-    }
-    st<T>(C + i, s / (float)kk);
-  }
-  __syncthreads();
-}
-
 // Shared-memory layout of row_attn_kernel (byte offsets), shared by host and device.
 constexpr int kAttnTok = 2;            // tokens per CTA iteration
 constexpr int kAttnThreads = 384;      // 12 warps: per token 1 (hx_moe) + 1 (x_moe) + 4 (cx_moe)
@@ -540,32 +453,83 @@ ONE_DEVINL void warp_gate_factors(float* g, int r, const float* ex, int E, float
 }
 
 // Per-expert partial sums over x[i0..i1) of rnd(rnd(x * c_e) + bias2[e, i]) for experts
-// e0..e0+7, reduced over the warp (exact fp64). Result valid in every lane.
+// e0..e0+7, reduced over the warp (exact fp64). Result valid in every lane. bf16 with even
+// bounds and 4-byte aligned rows: each lane takes input pairs, reads bias2 as bf16x2 and
+// rounds both sums with one packed conversion. The terms are bf16 numbers, so their fp64
+// sum is exact in any order and the result does not depend on the pairing.
 template <typename T>
 ONE_DEVINL void warp_expert_sums(const float* x, int i0, int i1, const T* B2, int in, const float* c, int e0, int E,
                                  double (&acc)[8]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.0;
-  for (int i = i0 + lane; i < i1; i += 32) {
-    const float xi = x[i];
+  const int ne = min(8, E - e0);
+  if (sizeof(T) == 2 && ((i0 | i1 | in) & 1) == 0 && (reinterpret_cast<uintptr_t>(B2) & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 7) == 0) {
+    float ce[8];
+    const uint32_t* brow[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (e0 + e < E) {
-        const float ce = c[e0 + e];
-        const float xc = ce == 1.0f ? xi : rnd<T>(xi * ce);
-        acc[e] += (double)rnd<T>(xc + ld<T>(B2 + (size_t)(e0 + e) * in + i));
-      }
+    for (int e = 0; e < 8; ++e) {
+      ce[e] = e < ne ? c[e0 + e] : 1.0f;
+      brow[e] = reinterpret_cast<const uint32_t*>(B2 + (size_t)(e0 + (e < ne ? e : 0)) * in);
+    }
+    for (int i = i0 + 2 * lane; i < i1; i += 64) {
+      const float2 xv = *reinterpret_cast<const float2*>(x + i);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < ne) {
+          float2 xc = xv;
+          if (ce[e] != 1.0f) {
+            const uint32_t q = pack_bf16x2(xv.x * ce[e], xv.y * ce[e]);
+            xc = make_float2(__uint_as_float(q << 16), __uint_as_float(q & 0xffff0000u));
+          }
+          const uint32_t bw = brow[e][i >> 1];
+          const uint32_t r = pack_bf16x2(xc.x + __uint_as_float(bw << 16), xc.y + __uint_as_float(bw & 0xffff0000u));
+          acc[e] += (double)__uint_as_float(r << 16);
+          acc[e] += (double)__uint_as_float(r & 0xffff0000u);
+        }
+    }
+  } else {
+    for (int i = i0 + lane; i < i1; i += 32) {
+      const float xi = x[i];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e0 + e < E) {
+          const float cv = c[e0 + e];
+          const float xc = cv == 1.0f ? xi : rnd<T>(xi * cv);
+          acc[e] += (double)rnd<T>(xc + ld<T>(B2 + (size_t)(e0 + e) * in + i));
+        }
+    }
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
 }
 
-// mean of the selected biased inputs over x[i0..i1) (one/linear_moe.py:87-90)
+// mean of the selected biased inputs over x[i0..i1) (one/linear_moe.py:87-90): fp32 sum in
+// selection order, divided by k, rounded once
 template <typename T>
 ONE_DEVINL void warp_combine(const float* x, int i0, int i1, const T* B2, int in, const float* c, const int* sel, int kk,
                              T* out) {
   const int lane = threadIdx.x & 31;
+  if (sizeof(T) == 2 && ((i0 | i1 | in) & 1) == 0 && (reinterpret_cast<uintptr_t>(B2) & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
+    for (int i = i0 + 2 * lane; i < i1; i += 64) {
+      const float2 xv = *reinterpret_cast<const float2*>(x + i);
+      float s0 = 0.f, s1 = 0.f;
+      for (int j = 0; j < kk; ++j) {
+        const int e = sel[j];
+        const float ce = c[e];
+        const uint32_t q = pack_bf16x2(xv.x * ce, xv.y * ce);
+        const uint32_t bw = *reinterpret_cast<const uint32_t*>(B2 + (size_t)e * in + i);
+        const uint32_t r = pack_bf16x2(__uint_as_float(q << 16) + __uint_as_float(bw << 16),
+                                       __uint_as_float(q & 0xffff0000u) + __uint_as_float(bw & 0xffff0000u));
+        s0 += __uint_as_float(r << 16);
+        s1 += __uint_as_float(r & 0xffff0000u);
+      }
+      *reinterpret_cast<uint32_t*>(out + i) = pack_bf16x2(s0 / (float)kk, s1 / (float)kk);
+    }
+    return;
+  }
   for (int i = i0 + lane; i < i1; i += 32) {
     float s2 = 0.f;
     for (int j = 0; j < kk; ++j) {
@@ -989,29 +953,88 @@ __global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttn
   }
 }
 
-// LinearMoE router alone (standalone op): per token, clamp the input (:53), then the
-// router of cta_router. gate logits come precomputed in R.glog.
+// Standalone LinearMoE router (one/linear_moe.py:53-90) on precomputed gate logits: one warp
+// per token, grid-stride, with the same steps and rounding as the decode path's routers
+// (warp_gate_factors, warp_expert_sums, topk_select, warp_combine). bias2 (when it fits) and
+// the clamped experts are staged once per CTA; each warp keeps its token's clamped input, gate
+// values, expert factors, scores and selection in its own slice of shared memory.
+constexpr int kRouterWarps = 8;
+constexpr size_t kRouterStageB2Max = 48 * 1024;
+struct RouterSmem {
+  size_t b2, ex, warp0, per_warp, total;
+  bool stage_b2;
+};
+__host__ __device__ inline RouterSmem router_smem(int in, int r, int E, int es) {
+  RouterSmem L;
+  const size_t b2 = (size_t)E * in * es;
+  L.stage_b2 = b2 <= kRouterStageB2Max;
+  L.b2 = 0;
+  L.ex = (L.stage_b2 ? (b2 + 15) & ~size_t(15) : 0);
+  L.warp0 = L.ex + (size_t)kMaxExperts * 4;
+  // 32 doubles of scratch, x [in], gate [r], factors [E], scores [E], selection [E]
+  L.per_warp = ((256 + (size_t)(in + r + 3 * kMaxExperts) * 4) + 15) & ~size_t(15);
+  L.total = L.warp0 + kRouterWarps * L.per_warp;
+  return L;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(128) moe_router_kernel(const MoeRouter R, int ntok, int r, int E, int k) {
-  extern __shared__ float sm[];
-  float* xs = sm;                   // [in]
-  float* gl = xs + R.in;            // [r]
-  float* cvals = gl + r;            // [E]
-  float* score = cvals + kMaxExperts;
-  int* sel = reinterpret_cast<int*>(score + kMaxExperts);
-  double* red = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(sel + kMaxExperts) + 7) & ~uintptr_t(7));
+__global__ void __launch_bounds__(32 * kRouterWarps) moe_router_kernel(const MoeRouter R, int ntok, int r, int E, int k) {
+  extern __shared__ __align__(16) uint8_t rsm[];
+  const int in = R.in, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const RouterSmem L = router_smem(in, r, E, (int)sizeof(T));
+  float* ex = reinterpret_cast<float*>(rsm + L.ex);
+  uint8_t* wb = rsm + L.warp0 + warp * L.per_warp;
+  double* cp = reinterpret_cast<double*>(wb);
+  float* xs = reinterpret_cast<float*>(wb + 256);
+  float* g = xs + in;
+  float* c = g + r;
+  float* sc = c + kMaxExperts;
+  int* sel = reinterpret_cast<int*>(sc + kMaxExperts);
   pdl_wait();
-  for (int t = blockIdx.x; t < ntok; t += gridDim.x) {
+  const T* B2 = reinterpret_cast<const T*>(R.bias2);
+  if (L.stage_b2) {
+    constexpr int VE = 16 / (int)sizeof(T);
+    T* b2s = reinterpret_cast<T*>(rsm + L.b2);
+    const int nv = E * in / VE;
+    if ((E * in) % VE == 0 && (reinterpret_cast<uintptr_t>(B2) & 15) == 0)
+      for (int v = threadIdx.x; v < nv; v += blockDim.x)
+        reinterpret_cast<uint4*>(b2s)[v] = reinterpret_cast<const uint4*>(B2)[v];
+    else
+      for (int v = threadIdx.x; v < E * in; v += blockDim.x) b2s[v] = B2[v];
+    B2 = b2s;
+  }
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    ex[e] = fminf(fmaxf(ld<T>(reinterpret_cast<const T*>(R.experts) + e), -10.f), 10.f);
+  __syncthreads();
+  const int kk = min(k, E);
+  for (int t = blockIdx.x * kRouterWarps + warp; t < ntok; t += gridDim.x * kRouterWarps) {
     const T* X = reinterpret_cast<const T*>(R.x) + (size_t)t * R.ldx;
-    for (int i = threadIdx.x; i < R.in; i += blockDim.x) xs[i] = fminf(fmaxf(ld<T>(X + i), -1e4f), 1e4f);
-    __syncthreads();
-    cta_router<T>(r, E, k, R, t, xs, gl, cvals, red, score, sel);
+    for (int i = lane; i < in; i += 32) xs[i] = fminf(fmaxf(ld<T>(X + i), -1e4f), 1e4f);  // (:53)
+    const T* G = reinterpret_cast<const T*>(R.glog) + (size_t)t * r;
+    for (int j = lane; j < r; j += 32) g[j] = ld<T>(G + j);
+    __syncwarp();
+    warp_gate_factors<T>(g, r, ex, E, c, cp);  // softmax (:56), expert factors (:59-68)
+    for (int e0 = 0; e0 < E; e0 += 8) {        // exact per-expert sums (:71-80)
+      double acc[8];
+      warp_expert_sums<T>(xs, 0, in, B2, in, c, e0, E, acc);
+      if (lane == 0)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e0 + e < E) sc[e0 + e] = rnd<T>(__double2float_rn(acc[e]));
+    }
+    __syncwarp();
+    if (lane == 0) {  // top-k (:83-84)
+      topk_select(sc, E, kk, sel);
+      if (R.idx_out)
+        for (int j = 0; j < kk; ++j) R.idx_out[(size_t)t * kk + j] = sel[j];
+    }
+    __syncwarp();
+    warp_combine<T>(xs, 0, in, B2, in, c, sel, kk, reinterpret_cast<T*>(R.comb) + (size_t)t * in);  // (:87-90)
+    __syncwarp();
   }
 }
 
-inline size_t moe_router_smem_bytes(int in, int r) {
-  return (size_t)(in + r + 2 * kMaxExperts) * 4 + (kMaxExperts + 2) * 4 + 8 + 4 * 8 * 8;
-}
+inline size_t moe_router_smem_bytes(int in, int r, int E, int es) { return router_smem(in, r, E, es).total; }
 
 
 }  // namespace one
