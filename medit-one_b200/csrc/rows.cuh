@@ -953,15 +953,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttn
   }
 }
 
-// Standalone LinearMoE router (one/linear_moe.py:53-90) on precomputed gate logits: one warp
-// per token, grid-stride, with the same steps and rounding as the decode path's routers
-// (warp_gate_factors, warp_expert_sums, topk_select, warp_combine). bias2 (when it fits) and
-// the clamped experts are staged once per CTA; each warp keeps its token's clamped input, gate
-// values, expert factors, scores and selection in its own slice of shared memory.
-constexpr int kRouterWarps = 8;
+// Standalone LinearMoE router (one/linear_moe.py:53-90) on precomputed gate logits, with the
+// same steps and rounding as the decode path's routers (warp_gate_factors, warp_expert_sums,
+// topk_select, warp_combine). Each warp takes groups of `group` (<= 32) tokens: for every token of
+// the group it computes the expert factors and scores; then the group's selections run
+// side by side, one token per lane (the selection is a sequential algorithm whose output
+// order matters, so it is parallelised across tokens, not within one); then each token's
+// biased inputs are combined. bias2 (when it fits) and the clamped experts are staged once
+// per CTA; per warp: one token's clamped input and gate values, and the group's factors,
+// scores and selections.
 constexpr size_t kRouterStageB2Max = 48 * 1024;
 struct RouterSmem {
-  size_t b2, ex, warp0, per_warp, total;
+  size_t b2, ex, warp0, per_warp, total, xs, g, cf, sc, sel;
+  int warps;
   bool stage_b2;
 };
 __host__ __device__ inline RouterSmem router_smem(int in, int r, int E, int es) {
@@ -971,25 +975,32 @@ __host__ __device__ inline RouterSmem router_smem(int in, int r, int E, int es) 
   L.b2 = 0;
   L.ex = (L.stage_b2 ? (b2 + 15) & ~size_t(15) : 0);
   L.warp0 = L.ex + (size_t)kMaxExperts * 4;
-  // 32 doubles of scratch, x [in], gate [r], factors [E], scores [E], selection [E]
-  L.per_warp = ((256 + (size_t)(in + r + 3 * kMaxExperts) * 4) + 15) & ~size_t(15);
-  L.total = L.warp0 + kRouterWarps * L.per_warp;
+  // per warp: 32 doubles of scratch, x [in], gate [r], group factors / scores / selections [32][E]
+  L.xs = 256;
+  L.g = L.xs + (size_t)in * 4;
+  L.cf = L.g + (size_t)r * 4;
+  L.sc = L.cf + (size_t)32 * E * 4;
+  L.sel = L.sc + (size_t)32 * E * 4;
+  L.per_warp = (L.sel + (size_t)32 * E * 4 + 15) & ~size_t(15);
+  const size_t budget = 200 * 1024 - L.warp0;
+  L.warps = (int)(budget / L.per_warp < 8 ? budget / L.per_warp : 8);
+  L.total = L.warp0 + (size_t)(L.warps > 0 ? L.warps : 1) * L.per_warp;
   return L;
 }
 
 template <typename T>
-__global__ void __launch_bounds__(32 * kRouterWarps) moe_router_kernel(const MoeRouter R, int ntok, int r, int E, int k) {
+__global__ void __launch_bounds__(256) moe_router_kernel(const MoeRouter R, int ntok, int r, int E, int k, int group) {
   extern __shared__ __align__(16) uint8_t rsm[];
-  const int in = R.in, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int in = R.in, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
   const RouterSmem L = router_smem(in, r, E, (int)sizeof(T));
   float* ex = reinterpret_cast<float*>(rsm + L.ex);
   uint8_t* wb = rsm + L.warp0 + warp * L.per_warp;
   double* cp = reinterpret_cast<double*>(wb);
-  float* xs = reinterpret_cast<float*>(wb + 256);
-  float* g = xs + in;
-  float* c = g + r;
-  float* sc = c + kMaxExperts;
-  int* sel = reinterpret_cast<int*>(sc + kMaxExperts);
+  float* xs = reinterpret_cast<float*>(wb + L.xs);
+  float* g = reinterpret_cast<float*>(wb + L.g);
+  float* cf = reinterpret_cast<float*>(wb + L.cf);  // [32][E] expert factors of the group
+  float* sc = reinterpret_cast<float*>(wb + L.sc);  // [32][E] expert scores
+  int* sel = reinterpret_cast<int*>(wb + L.sel);    // [32][E] chosen experts
   pdl_wait();
   const T* B2 = reinterpret_cast<const T*>(R.bias2);
   if (L.stage_b2) {
@@ -1007,34 +1018,49 @@ __global__ void __launch_bounds__(32 * kRouterWarps) moe_router_kernel(const Moe
     ex[e] = fminf(fmaxf(ld<T>(reinterpret_cast<const T*>(R.experts) + e), -10.f), 10.f);
   __syncthreads();
   const int kk = min(k, E);
-  for (int t = blockIdx.x * kRouterWarps + warp; t < ntok; t += gridDim.x * kRouterWarps) {
+  auto load_x = [&](int t) {
     const T* X = reinterpret_cast<const T*>(R.x) + (size_t)t * R.ldx;
     for (int i = lane; i < in; i += 32) xs[i] = fminf(fmaxf(ld<T>(X + i), -1e4f), 1e4f);  // (:53)
-    const T* G = reinterpret_cast<const T*>(R.glog) + (size_t)t * r;
-    for (int j = lane; j < r; j += 32) g[j] = ld<T>(G + j);
-    __syncwarp();
-    warp_gate_factors<T>(g, r, ex, E, c, cp);  // softmax (:56), expert factors (:59-68)
-    for (int e0 = 0; e0 < E; e0 += 8) {        // exact per-expert sums (:71-80)
-      double acc[8];
-      warp_expert_sums<T>(xs, 0, in, B2, in, c, e0, E, acc);
-      if (lane == 0)
+  };
+  group = max(1, min(32, group));
+  for (int t0 = (blockIdx.x * nwarp + warp) * group; t0 < ntok; t0 += gridDim.x * nwarp * group) {
+    const int nt = min(group, ntok - t0);
+    for (int u = 0; u < nt; ++u) {
+      const int t = t0 + u;
+      load_x(t);
+      const T* G = reinterpret_cast<const T*>(R.glog) + (size_t)t * r;
+      for (int j = lane; j < r; j += 32) g[j] = ld<T>(G + j);
+      __syncwarp();
+      float* c = cf + u * E;
+      warp_gate_factors<T>(g, r, ex, E, c, cp);  // softmax (:56), expert factors (:59-68)
+      for (int e0 = 0; e0 < E; e0 += 8) {        // exact per-expert sums (:71-80)
+        double acc[8];
+        warp_expert_sums<T>(xs, 0, in, B2, in, c, e0, E, acc);
+        if (lane == 0)
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (e0 + e < E) sc[e0 + e] = rnd<T>(__double2float_rn(acc[e]));
+          for (int e = 0; e < 8; ++e)
+            if (e0 + e < E) sc[u * E + e0 + e] = rnd<T>(__double2float_rn(acc[e]));
+      }
+      __syncwarp();
     }
-    __syncwarp();
-    if (lane == 0) {  // top-k (:83-84)
-      topk_select(sc, E, kk, sel);
+    if (lane < nt) {  // top-k (:83-84), one token per lane
+      topk_select(sc + lane * E, E, kk, sel + lane * E);
       if (R.idx_out)
-        for (int j = 0; j < kk; ++j) R.idx_out[(size_t)t * kk + j] = sel[j];
+        for (int j = 0; j < kk; ++j) R.idx_out[(size_t)(t0 + lane) * kk + j] = sel[lane * E + j];
     }
     __syncwarp();
-    warp_combine<T>(xs, 0, in, B2, in, c, sel, kk, reinterpret_cast<T*>(R.comb) + (size_t)t * in);  // (:87-90)
-    __syncwarp();
+    for (int u = 0; u < nt; ++u) {  // mean of the chosen biased inputs (:87-90)
+      load_x(t0 + u);
+      __syncwarp();
+      warp_combine<T>(xs, 0, in, B2, in, cf + u * E, sel + u * E, kk,
+                      reinterpret_cast<T*>(R.comb) + (size_t)(t0 + u) * in);
+      __syncwarp();
+    }
   }
 }
 
 inline size_t moe_router_smem_bytes(int in, int r, int E, int es) { return router_smem(in, r, E, es).total; }
+inline int moe_router_warps(int in, int r, int E, int es) { return router_smem(in, r, E, es).warps; }
 
 
 }  // namespace one
