@@ -1,7 +1,7 @@
 """Decode throughput of the 140M-class MedIT One model in bf16 on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
-                    [--workload decode|attention|linear_moe]
+                    [--workload decode|attention|linear_moe|prefill]
 
 Workload (per GPU, weak scaling): 256 sequences, prompt of 128 tokens (ids uniform in
 [0, 32000), seed 4 + rank), then greedy single-token decode steps carrying the
@@ -456,6 +456,139 @@ def run_attention_reference(args):
     print(json.dumps(line), flush=True)
 
 
+PF_B, PF_S, PF_SEED = 64, 4096, 5
+PF_METRIC = "prefill tok/s (140M-class bf16, 4096-token prompts, 64 sequences per call)"
+
+
+def gemm_flops_per_token(cfg) -> float:
+    """2 x the weights a token's forward multiplies (lm_head excluded: prefill returns no logits)."""
+    return step_bytes(cfg, 1)["flops"] - 2.0 * cfg.vocab_size * cfg.hidden_size
+
+
+def prefill_cpu(cfg, seqs: int, length: int) -> dict:
+    """The reference forward (oracle restatement of one/modeling_one.py:671-826) on the host
+    CPU for a bounded sample of the prompts."""
+    from one.initialization import init_state_dict
+    from oracle import one_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    sd = init_state_dict(cfg, SEED, torch.bfloat16)
+    oc = O.OracleConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size, transformer_dim=cfg.transformer_dim,
+                        num_hidden_layers=cfg.num_hidden_layers, num_attention_heads=cfg.num_attention_heads,
+                        head_dim=cfg.head_dim, intermediate_size=cfg.intermediate_size, num_experts=cfg.num_experts,
+                        top_k_experts=cfg.top_k_experts, r=cfg.r)
+    g = torch.Generator().manual_seed(PF_SEED)
+    ids = torch.randint(0, cfg.vocab_size, (seqs, length), generator=g)
+    with torch.no_grad():
+        O.forward(sd, ids[:, :16], oc, torch.bfloat16)  # warm-up
+        t0 = time.perf_counter()
+        O.forward(sd, ids, oc, torch.bfloat16)
+        dt = time.perf_counter() - t0
+    return {"value": seqs * length / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "seconds": dt, "sample": f"{seqs} prompts x {length} tokens (oracle restatement of the reference's "
+                                     f"forward, bf16)"}
+
+
+def prefill_launches(cfg) -> int:
+    """Kernels of one prefill call: per layer row_pre, prefix-mean scan, GEMM A, attention/routers,
+    GEMM C, gate/up, down; then row_pre, up_scaler, row_norm, lm_head (+argmax of each prompt's
+    last position), the counter update."""
+    return cfg.num_hidden_layers * 7 + 5
+
+
+def run_prefill(args, ws, rank, local):
+    """One step = prefill of 64 prompts of 4096 tokens (the per-GPU share of the 4096 x 4096 prompt
+    set is 512 prompts: 8 steps); then the decode rate at batch 64 from that state."""
+    from one.configuration_one import config_140m
+    from one.engine import OneEngine
+    from one.initialization import init_state_dict
+    cfg = config_140m()
+    dev = f"cuda:{local}"
+    dsteps = 200
+    eng = OneEngine(cfg, init_state_dict(cfg, SEED, torch.bfloat16), dev, torch.bfloat16, max_batch=PF_B,
+                    max_tokens=PF_B * PF_S, hist_cap=dsteps + 64, max_positions=PF_S + dsteps + 64)
+    g = torch.Generator().manual_seed(PF_SEED + rank)
+    ids = torch.randint(0, cfg.vocab_size, (PF_B, PF_S), generator=g)
+    ids_dev = ids.to(dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        eng.prefill(ids_dev)
+    torch.cuda.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            eng.prefill(ids_dev)
+        e1.record(stream)
+        e1.synchronize()
+    ms = max_over_ranks(ws, e0.elapsed_time(e1))
+    if eng.device_error() != (0, 0):
+        raise RuntimeError(f"device error {eng.device_error()}")
+    tokens = PF_B * PF_S
+    value = ws * tokens * args.steps / (ms / 1000.0)
+    fl = gemm_flops_per_token(cfg) * tokens
+    # decode at batch 64 from the prefilled state (positions 4096 ..)
+    eng.capture(1)
+    for _ in range(5):
+        eng.replay()
+    torch.cuda.synchronize()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    for _ in range(dsteps):
+        eng.replay()
+    d1.record(stream)
+    d1.synchronize()
+    dec_ms = d0.elapsed_time(d1) / dsteps
+    # e2e through the public API: prompt ids from pinned host memory in, each prompt's next token out
+    hids = ids.pin_memory()
+    barrier(ws)
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(args.steps):
+        lg = eng.prefill(hids.to(dev, non_blocking=True), logits="last")
+        nxt = lg.argmax(-1).to(torch.int32).cpu()
+    x1.record(stream)
+    x1.synchronize()
+    e_ms = max_over_ranks(ws, x0.elapsed_time(x1))
+    e2e = ws * tokens * args.steps / (e_ms / 1000.0)
+    assert nxt.shape[0] == PF_B
+    _, _, tf_sus, src = peaks()
+    t_step = ms / 1000.0 / args.steps
+    clocks = clk.summary()
+    if rank == 0:
+        line = {"metric": PF_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init weights N(0,0.02) seed 4, prompt ids uniform, seed 5 + rank)",
+                "config": {"workload": "140M-class One bf16 prompt ingestion, 64 prompts x 4096 tokens per call "
+                                       "(the per-GPU 512-prompt share of 4096 x 4096 is 8 calls), then greedy "
+                                       "decode at batch 64",
+                           "decode_b64_ms_per_step": dec_ms, "decode_b64_tok_s": ws * PF_B / (dec_ms / 1000.0),
+                           "l2": "inputs larger than L2 (weights 285 MB, activations GBs)"},
+                "roofline": {"bound": "tensor", "kernel": "prefill (tcgen05 GEMMs + row kernels)",
+                             "achieved": fl / t_step / 1e12, "peak": tf_sus, "unit": "TFLOP/s",
+                             "frac": fl / t_step / 1e12 / tf_sus, "peak_source": src + " (sustained)",
+                             "traffic": None, "flops_per_token": gemm_flops_per_token(cfg)},
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": tokens * 8, "d2h_bytes_per_step": PF_B * 4},
+                "gpu_launches": args.steps * prefill_launches(cfg), "clocks": clocks}
+        if ws == 1 and not args.no_cpu_baseline:
+            r = prefill_cpu(cfg, 8, 1024)
+            line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+
+
+def run_prefill_reference(args):
+    from one.configuration_one import config_140m
+    r = prefill_cpu(config_140m(), 8, 1024)
+    line = {"impl": "reference", "metric": PF_METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": 1, "warmup": 1, "ms_per_step": 1000 * r["seconds"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, uniform prompt ids)",
+            "config": {"workload": "140M-class One bf16 prompt ingestion"},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 MOE_T, MOE_D, MOE_E, MOE_K, MOE_R = 16384, 768, 8, 2, 64
 MOE_METRIC = "LinearMoE TFLOP/s (16384 x 768 bf16, 8 experts top-2, r 64, 768 -> 768)"
 
@@ -608,9 +741,9 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe", "prefill"],
                     help="decode: the 140M decode step (default); attention: the isolated RoPE + attention op; "
-                         "linear_moe: the isolated LinearMoE op on 16384 tokens")
+                         "linear_moe: the isolated LinearMoE op on 16384 tokens; prefill: 64 x 4096-token prompts")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
@@ -622,6 +755,8 @@ def main():
                 run_attention_reference(args)
             elif args.workload == "linear_moe":
                 run_linear_moe_reference(args)
+            elif args.workload == "prefill":
+                run_prefill_reference(args)
             else:
                 run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), 0)
         return
@@ -631,6 +766,8 @@ def main():
             run_attention(args, ws, rank, local)
         elif args.workload == "linear_moe":
             run_linear_moe(args, ws, rank, local)
+        elif args.workload == "prefill":
+            run_prefill(args, ws, rank, local)
         else:
             run_native(args, ws, rank, local)
     finally:
