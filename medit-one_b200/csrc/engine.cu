@@ -151,6 +151,7 @@ __global__ void next_ids_kernel(const NextIdsParams p) {
 struct Launch {
   LaunchKind kind;
   int bn = 0;  // tensor-core tile width
+  int minb = 1;  // row_attn: CTAs per SM the instantiation is compiled for
   int grid = 1, block = 1;
   size_t smem = 0;
   int dtype = ONE_DTYPE_BF16;
@@ -304,6 +305,8 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::kSmem));
   const int attn_max = 220 * 1024;
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
+  CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          attn_max));
   CK(cudaFuncSetAttribute(row_attn_kernel<float, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(row_attn_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
@@ -347,7 +350,9 @@ static int run(const Launch& L, cudaStream_t st) {
     case L_ROW_PRE: e = bf ? launch_row_pre<__nv_bfloat16>(L, st) : launch_row_pre<float>(L, st); break;
     case L_ROW_NORM: e = bf ? launch_row_norm<__nv_bfloat16>(L, st) : launch_row_norm<float>(L, st); break;
     case L_ROW_ATTN:
-      if (L.nv == 16)
+      if (L.nv == 16 && bf && L.minb == 2)
+        e = launch_k(row_attn_kernel<__nv_bfloat16, 16, 2>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra);
+      else if (L.nv == 16)
         e = bf ? launch_k(row_attn_kernel<__nv_bfloat16, 16>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra)
                : launch_k(row_attn_kernel<float, 16>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra);
       else
@@ -654,7 +659,7 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       s.kind = L_SCAN;
       s.dtype = dt;
       s.block = 256;
-      s.grid = (batch * D + 255) / 256;
+      s.grid = (batch * (D / 2) + 255) / 256;  // one thread per (sequence, feature pair)
       s.sc = ScanParams{batch, seq_len, D, B_(e->b.norm_x), B_(e->b.mean),
                         e->at<float>(e->b.state) + (size_t)l * e->max_batch * D, prompt_div};
       plan.push_back(s);
@@ -687,6 +692,10 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       a.grid = std::min((T + kAttnTok - 1) / kAttnTok, num_sms() * 2);
       a.nv = H <= 16 ? 16 : 64;
       a.smem = attn_layout(H, Dh, c.r, c.num_experts, D, moe ? 1 : 0, es).total;
+      // prompt ingestion (more token pairs than one CTA per SM covers): two CTAs per SM
+      if (!decode && dt == ONE_DTYPE_BF16 && a.nv == 16 && 2 * (a.smem + 1024) <= 227 * 1024 &&
+          (T + kAttnTok - 1) / kAttnTok > num_sms())
+        a.minb = 2;
       if (a.smem > 220 * 1024) return fail(ONE_ERR_UNSUPPORTED, "attention/router weights exceed shared memory (%zu B)", a.smem);
       if (moe && (HH % 8 || D % 8 || (c.r * HH) % 8 || Dh % 8))
         return fail(ONE_ERR_UNSUPPORTED, "router shapes: H*H, D and head_dim must be multiples of 8");

@@ -281,17 +281,37 @@ template <typename T>
 __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
   pdl_launch_dependents();
   pdl_wait();
+  // one thread per (sequence, feature pair): the prefix sum runs in token order in fp32 (the
+  // reference's CPU cumsum order), with the next 32 tokens' inputs loaded ahead of the adds
+  constexpr int kAhead = 32;
+  const int half = p.D / 2;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= p.B * p.D) return;
-  const int bb = idx / p.D, d = idx % p.D;
-  float acc = p.state[idx];
-  const T* x = reinterpret_cast<const T*>(p.norm_x) + (size_t)bb * p.S * p.D + d;
-  T* m = reinterpret_cast<T*>(p.mean) + (size_t)bb * p.S * p.D + d;
-  for (int s = 0; s < p.S; ++s) {
-    acc += ld<T>(x + (size_t)s * p.D);
-    st<T>(m + (size_t)s * p.D, rnd<T>(acc) / p.div[s]);
+  if (idx >= p.B * half) return;
+  const int bb = idx / half, d = 2 * (idx % half);
+  float a0 = p.state[(size_t)bb * p.D + d], a1 = p.state[(size_t)bb * p.D + d + 1];
+  const T* __restrict__ x = reinterpret_cast<const T*>(p.norm_x) + (size_t)bb * p.S * p.D + d;
+  T* __restrict__ m = reinterpret_cast<T*>(p.mean) + (size_t)bb * p.S * p.D + d;
+  for (int s0 = 0; s0 < p.S; s0 += kAhead) {
+    const int n = min(kAhead, p.S - s0);
+    float v0[kAhead], v1[kAhead];
+#pragma unroll
+    for (int j = 0; j < kAhead; ++j)
+      if (j < n) {
+        v0[j] = ld<T>(x + (size_t)(s0 + j) * p.D);
+        v1[j] = ld<T>(x + (size_t)(s0 + j) * p.D + 1);
+      }
+#pragma unroll
+    for (int j = 0; j < kAhead; ++j)
+      if (j < n) {
+        a0 += v0[j];
+        a1 += v1[j];
+        const float dv = p.div[s0 + j];
+        st<T>(m + (size_t)(s0 + j) * p.D, rnd<T>(a0) / dv);
+        st<T>(m + (size_t)(s0 + j) * p.D + 1, rnd<T>(a1) / dv);
+      }
   }
-  p.state[idx] = acc;
+  p.state[(size_t)bb * p.D + d] = a0;
+  p.state[(size_t)bb * p.D + d + 1] = a1;
 }
 
 // ------------------------------------------------------------------ final norm
@@ -550,8 +570,10 @@ ONE_DEVINL void warp_combine(const float* x, int i0, int i1, const T* B2, int in
 //   phase B: per token, warp 0 routes hx_moe, warp 1 x_moe (gate GEMV, softmax, expert
 //            factors, expert sums, top-k, combine) and warps 2..5 route cx_moe, each
 //            summing and combining a quarter of the 768 inputs; no CTA-wide barrier.
-template <typename T, int HMAX>
-__global__ void __launch_bounds__(kAttnThreads, 1) row_attn_kernel(const RowAttnParams p) {
+// MINB = 2 (prompt ingestion): two CTAs per SM, registers capped to fit both; decode keeps
+// MINB = 1 for the shortest per-token chain.
+template <typename T, int HMAX, int MINB = 1>
+__global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowAttnParams p) {
   extern __shared__ __align__(16) uint8_t smb[];
   const int H = p.H, Dh = p.Dh, HD = H * Dh, HH = H * H, r = p.r, E = p.E;
   const int D = p.use_moe ? p.rt[2].in : 0;
