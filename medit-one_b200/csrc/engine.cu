@@ -691,11 +691,15 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       a.block = kAttnThreads;
       a.grid = std::min((T + kAttnTok - 1) / kAttnTok, num_sms() * 2);
       a.nv = H <= 16 ? 16 : 64;
-      a.smem = attn_layout(H, Dh, c.r, c.num_experts, D, moe ? 1 : 0, es).total;
-      // prompt ingestion (more token pairs than one CTA per SM covers): two CTAs per SM
-      if (!decode && dt == ONE_DTYPE_BF16 && a.nv == 16 && 2 * (a.smem + 1024) <= 227 * 1024 &&
-          (T + kAttnTok - 1) / kAttnTok > num_sms())
+      a.smem = attn_layout(H, Dh, c.r, c.num_experts, D, moe ? 1 : 0, es, 1).total;
+      // prompt ingestion (more token pairs than one CTA per SM covers): two CTAs per SM,
+      // without the staged projection / gate weights
+      const size_t smem2 = attn_layout(H, Dh, c.r, c.num_experts, D, moe ? 1 : 0, es, 0).total;
+      if (!decode && dt == ONE_DTYPE_BF16 && a.nv == 16 && 2 * (smem2 + 1024) <= 227 * 1024 &&
+          (T + kAttnTok - 1) / kAttnTok > num_sms()) {
         a.minb = 2;
+        a.smem = smem2;
+      }
       if (a.smem > 220 * 1024) return fail(ONE_ERR_UNSUPPORTED, "attention/router weights exceed shared memory (%zu B)", a.smem);
       if (moe && (HH % 8 || D % 8 || (c.r * HH) % 8 || Dh % 8))
         return fail(ONE_ERR_UNSUPPORTED, "router shapes: H*H, D and head_dim must be multiples of 8");

@@ -382,6 +382,8 @@ struct AttnTokLayout {
 };
 struct AttnLayout {
   int wqkv, bqkv, gate, gate_ld, experts, b2, tok0, total;
+  int wq16, g16;  // staged bf16 copies of lin_q/k/v [3][H][Dh] and the hx/x gates [2][r][HH] (0 bytes if not staged)
+  bool staged;
   AttnTokLayout tk;
 };
 __host__ __device__ inline int attn_take(int& off, int bytes) {
@@ -389,10 +391,17 @@ __host__ __device__ inline int attn_take(int& off, int bytes) {
   off = (off + bytes + 15) & ~15;
   return o;
 }
-__host__ __device__ inline AttnLayout attn_layout(int H, int Dh, int r, int E, int D, int use_moe, int es) {
+// stage_w: copy the tensor-core operands read by every token (lin_q/k/v, the hx/x gate
+// weights) into shared memory before the dependency wait (decode); prompt ingestion runs two
+// CTAs per SM and reads them through L1 instead.
+__host__ __device__ inline AttnLayout attn_layout(int H, int Dh, int r, int E, int D, int use_moe, int es,
+                                                  int stage_w = 0) {
   AttnLayout L;
   int off = 0;
   const int HD = H * Dh, HH = H * H, Dp = Dh + 4;
+  L.staged = stage_w && es == 2 && H <= 16;
+  L.wq16 = attn_take(off, L.staged ? 3 * HD * 2 : 0);
+  L.g16 = attn_take(off, L.staged && use_moe && HH % 16 == 0 ? 2 * r * HH * 2 : 0);
   L.wqkv = attn_take(off, (es == 4 || H > 16) ? 3 * H * Dp * 4 : 0);  // CUDA-core projections only
   L.bqkv = attn_take(off, 3 * H * 4);
   L.gate_ld = HH + (es == 2 ? 2 : 1);  // odd row stride in 32-bit words: conflict-free rows
@@ -578,7 +587,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
   const int H = p.H, Dh = p.Dh, HD = H * Dh, HH = H * H, r = p.r, E = p.E;
   const int D = p.use_moe ? p.rt[2].in : 0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nw = nthr >> 5;
-  const AttnLayout L = attn_layout(H, Dh, r, E, D, p.use_moe, (int)sizeof(T));
+  const AttnLayout L = attn_layout(H, Dh, r, E, D, p.use_moe, (int)sizeof(T), MINB == 1 ? 1 : 0);
   float* wqkv = reinterpret_cast<float*>(smb + L.wqkv);
   float* bqkv = reinterpret_cast<float*>(smb + L.bqkv);
   float* exps = reinterpret_cast<float*>(smb + L.experts);
@@ -586,6 +595,19 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
   const int inr[3] = {HH, HH, D};
 
   // ---- small weights to shared memory (not written by the previous kernel: before the wait)
+  if (L.staged) {
+    const uint4* src[3] = {reinterpret_cast<const uint4*>(p.wq), reinterpret_cast<const uint4*>(p.wk),
+                           reinterpret_cast<const uint4*>(p.wv)};
+    uint4* dst = reinterpret_cast<uint4*>(smb + L.wq16);
+    const int nv = HD * 2 / 16;  // 16-byte vectors per projection
+    for (int v = tid; v < 3 * nv; v += nthr) dst[v] = src[v / nv][v % nv];
+    if (p.use_moe && HH % 16 == 0) {
+      const int ng = r * HH * 2 / 16;
+      uint4* gd = reinterpret_cast<uint4*>(smb + L.g16);
+      for (int v = tid; v < 2 * ng; v += nthr)
+        gd[v] = reinterpret_cast<const uint4*>(p.rt[v / ng].gate_w)[v % ng];
+    }
+  }
   constexpr bool kTensor = sizeof(T) == 2;  // bf16: projections and gates on mma.sync
   if (!kTensor || H > 16)
     for (int v = tid; v < 3 * HD / 8; v += nthr) {
@@ -691,6 +713,9 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
           srcs[2] = reinterpret_cast<const float*>(tb + L.tk.row) + 2 * HD + h * Dh;
         }
         const T* Ws[3] = {reinterpret_cast<const T*>(p.wq), reinterpret_cast<const T*>(p.wk), reinterpret_cast<const T*>(p.wv)};
+        if (L.staged)
+#pragma unroll
+          for (int pj = 0; pj < 3; ++pj) Ws[pj] = reinterpret_cast<const T*>(smb + L.wq16) + pj * HD;
         float acc[3][2][4];
 #pragma unroll
         for (int pj = 0; pj < 3; ++pj)
@@ -854,7 +879,9 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
       const int g = lane >> 2, c = lane & 3;
       for (int nt = warp; nt < 2 * r / 8; nt += nw) {
         const int ri = (nt * 8) / r, j0 = nt * 8 - ri * r;
-        const T* W = reinterpret_cast<const T*>(p.rt[ri].gate_w) + (size_t)(j0 + g) * HH + 2 * c;
+        const T* Wr = L.staged ? reinterpret_cast<const T*>(smb + L.g16) + (size_t)ri * r * HH
+                               : reinterpret_cast<const T*>(p.rt[ri].gate_w);
+        const T* W = Wr + (size_t)(j0 + g) * HH + 2 * c;
         const float* xs = g < ntok ? reinterpret_cast<const float*>(smb + L.tok0 + g * L.tk.bytes + L.tk.xs) : nullptr;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int ks = 0; ks < HH; ks += 16) {
