@@ -609,7 +609,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
     }
   }
   constexpr bool kTensor = sizeof(T) == 2;  // bf16: projections and gates on mma.sync
-  if (!kTensor || H > 16)
+  if constexpr (!(kTensor && HMAX <= 16))
     for (int v = tid; v < 3 * HD / 8; v += nthr) {
       const int u = (v * 8) / Dh, d0 = (v * 8) % Dh, which = u / H;
       const T* W = reinterpret_cast<const T*>(which == 0 ? p.wq : which == 1 ? p.wk : p.wv);
@@ -681,8 +681,10 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
     __syncthreads();
 
     // ---- phase A
-    const bool mmaA = kTensor && H <= 16;
-    if (mmaA) {
+    // HMAX = 16 instantiations only run H <= 16: the CUDA-core path below is not compiled
+    // into them (instruction-cache pressure)
+    constexpr bool mmaA = kTensor && HMAX <= 16;
+    if constexpr (mmaA) {
       // warp per head, both tokens at once: RoPE into shared rows, then q|k|v = x @ W^T on
       // mma.sync (the tokens are the M rows of an m16n8k16 tile), bias, rounding, softmax.
       for (int h = warp; h < H; h += nw) {
