@@ -29,9 +29,9 @@ static int router_launch(const MoeRouter& R, int n, int r, int E, int k, int dty
   const int grid = std::max(1, std::min((groups + warps - 1) / warps, num_sms() * per_sm));
   cudaError_t e = dtype == ONE_DTYPE_BF16
                       ? launch_k(moe_router_kernel<__nv_bfloat16>, dim3(grid), dim3(32 * warps), smem, st, R, n, r,
-                                 E, k, group)
+                                 E, k, group, topk_tie_selection(E, std::min(k, E)))
                       : launch_k(moe_router_kernel<float>, dim3(grid), dim3(32 * warps), smem, st, R, n, r, E, k,
-                                 group);
+                                 group, topk_tie_selection(E, std::min(k, E)));
   if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "router launch: %s", cudaGetErrorString(e));
   return ONE_OK;
 }

@@ -728,6 +728,7 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
         r2.gate_w = nullptr; r2.glog = B_(e->b.gcx); r2.experts = LW(ONE_W_CX_EXPERTS); r2.bias2 = LW(ONE_W_CX_BIAS2);
         r2.x = B_(e->b.cxc[cur]); r2.ldx = D; r2.in = D; r2.comb = B_(e->b.comb_cx); r2.idx_out = ridx + (size_t)2 * T * k;
       }
+      if (moe) q.tie = topk_tie_selection(c.num_experts, std::min(c.top_k, c.num_experts));
       q.err = err;
       plan.push_back(a);
     }

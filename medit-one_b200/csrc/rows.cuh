@@ -370,6 +370,7 @@ struct RowAttnParams {
   const void* wv; const void* bv;
   void* o;                // [T, H*H] attention output (plain-Linear path input), optional
   MoeRouter rt[3];        // hx_moe, x_moe, cx_moe
+  unsigned long long tie; // topk_tie_selection(E, k)
   DevErr* err;
 };
 
@@ -951,7 +952,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
           __syncwarp();
           if (lane == 0) {
             int chosen[kMaxExperts];
-            topk_select(sc + ri * E, E, kk, chosen);
+            topk_select_fast(sc + ri * E, E, kk, chosen, p.tie);
             for (int j = 0; j < kk; ++j) {
               sel[ri * E + j] = chosen[j];
               if (p.rt[ri].idx_out) p.rt[ri].idx_out[(size_t)t * kk + j] = chosen[j];
@@ -989,7 +990,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
               sc[2 * E + e] = rnd<T>(__double2float_rn(s2));
             }
             int chosen[kMaxExperts];
-            topk_select(sc + 2 * E, E, kk, chosen);
+            topk_select_fast(sc + 2 * E, E, kk, chosen, p.tie);
             for (int j = 0; j < kk; ++j) {
               sel[2 * E + j] = chosen[j];
               if (p.rt[2].idx_out) p.rt[2].idx_out[(size_t)t * kk + j] = chosen[j];
@@ -1025,7 +1026,6 @@ __host__ __device__ inline RouterSmem router_smem(int in, int r, int E, int es) 
   L.stage_b2 = b2 <= kRouterStageB2Max;
   L.b2 = 0;
   L.ex = (L.stage_b2 ? (b2 + 15) & ~size_t(15) : 0);
-  L.warp0 = L.ex + (size_t)kMaxExperts * 4;
   // per warp: 32 doubles of scratch, x [in], gate [r], group factors / scores / selections [32][E]
   L.xs = 256;
   L.g = L.xs + (size_t)in * 4;
@@ -1033,6 +1033,7 @@ __host__ __device__ inline RouterSmem router_smem(int in, int r, int E, int es) 
   L.sc = L.cf + (size_t)32 * E * 4;
   L.sel = L.sc + (size_t)32 * E * 4;
   L.per_warp = (L.sel + (size_t)32 * E * 4 + 15) & ~size_t(15);
+  L.warp0 = L.ex + (size_t)kMaxExperts * 4;
   const size_t budget = 200 * 1024 - L.warp0;
   L.warps = (int)(budget / L.per_warp < 8 ? budget / L.per_warp : 8);
   L.total = L.warp0 + (size_t)(L.warps > 0 ? L.warps : 1) * L.per_warp;
@@ -1040,7 +1041,8 @@ __host__ __device__ inline RouterSmem router_smem(int in, int r, int E, int es) 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) moe_router_kernel(const MoeRouter R, int ntok, int r, int E, int k, int group) {
+__global__ void __launch_bounds__(256) moe_router_kernel(const MoeRouter R, int ntok, int r, int E, int k, int group,
+                                                         unsigned long long tie) {
   extern __shared__ __align__(16) uint8_t rsm[];
   const int in = R.in, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
   const RouterSmem L = router_smem(in, r, E, (int)sizeof(T));
@@ -1095,7 +1097,7 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const MoeRouter R, int 
       __syncwarp();
     }
     if (lane < nt) {  // top-k (:83-84), one token per lane
-      topk_select(sc + lane * E, E, kk, sel + lane * E);
+      topk_select_fast(sc + lane * E, E, kk, sel + lane * E, tie);
       if (R.idx_out)
         for (int j = 0; j < kk; ++j) R.idx_out[(size_t)(t0 + lane) * kk + j] = sel[lane * E + j];
     }
