@@ -451,7 +451,7 @@ ONE_DEVINL void named_bar(int id, int nthreads) { asm volatile("bar.sync %0, %1;
 // factors c_e = 1 + silu(clamp(mean_r(rnd(g * e)))) (one/linear_moe.py:56-68) into c[].
 // One warp; `cp` is 32 doubles of scratch.
 template <typename T>
-ONE_DEVINL void warp_gate_factors(float* g, int r, const float* ex, int E, float* c, double* cp) {
+ONE_DEVINL void warp_gate_factors_loop(float* g, int r, const float* ex, int E, float* c, double* cp) {
   const int lane = threadIdx.x & 31;
   float mx = -INFINITY;
   for (int j = lane; j < r; j += 32) mx = fmaxf(mx, g[j]);
@@ -480,6 +480,64 @@ ONE_DEVINL void warp_gate_factors(float* g, int r, const float* ex, int E, float
     }
     __syncwarp();
   }
+}
+
+// Gate softmax (one/linear_moe.py:56) and expert factors c_e = 1 + silu(clamp(mean_j
+// rnd(gate_j * experts_e))) (:59-68) for one token, one warp. r <= 128: each lane keeps its gate
+// entries in registers, computes each exponential once, and accumulates the products for all
+// experts; the per-expert sums are exact (fp64 sums of bf16 terms), so the order of the
+// warp reduction does not change them. Larger r takes warp_gate_factors_loop.
+template <typename T>
+ONE_DEVINL void warp_gate_factors(float* g, int r, const float* ex, int E, float* c, double* cp) {
+  constexpr int kPer = 4;
+  if (r > 32 * kPer) {
+    warp_gate_factors_loop<T>(g, r, ex, E, c, cp);
+    return;
+  }
+  const int lane = threadIdx.x & 31;
+  float gv[kPer];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int m = 0; m < kPer; ++m) {
+    const int j = lane + 32 * m;
+    gv[m] = j < r ? g[j] : -INFINITY;
+    mx = fmaxf(mx, gv[m]);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int m = 0; m < kPer; ++m) {
+    gv[m] = lane + 32 * m < r ? expf(gv[m] - mx) : 0.f;
+    sum += gv[m];
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.0f / sum;
+#pragma unroll
+  for (int m = 0; m < kPer; ++m) gv[m] = rnd<T>(gv[m] * inv);
+  for (int e0 = 0; e0 < E; e0 += 8) {
+    double acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      acc[e] = 0.0;
+      if (e0 + e < E) {
+        const float xe = ex[e0 + e];
+#pragma unroll
+        for (int m = 0; m < kPer; ++m)
+          if (lane + 32 * m < r) acc[e] += (double)rnd<T>(gv[m] * xe);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
+    double mine = acc[0];
+#pragma unroll
+    for (int e = 1; e < 8; ++e)
+      if (lane == e) mine = acc[e];
+    if (lane < 8 && e0 + lane < E) {
+      const float scv = fminf(fmaxf(rnd<T>((float)mine / (float)r), -10.f), 10.f);
+      c[e0 + lane] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
+    }
+  }
+  __syncwarp();
 }
 
 // Per-expert partial sums over x[i0..i1) of rnd(rnd(x * c_e) + bias2[e, i]) for experts
@@ -641,43 +699,61 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
 
   for (int t0 = blockIdx.x * kAttnTok; t0 < p.T; t0 += gridDim.x * kAttnTok) {
     const int ntok = min(kAttnTok, p.T - t0);
-    // ---- phase 0: rows of each token
-    for (int k = 0; k < ntok; ++k) {
-      uint8_t* tb = smb + L.tok0 + k * L.tk.bytes;
-      float* row = reinterpret_cast<float*>(tb + L.tk.row);
-      float* cs = reinterpret_cast<float*>(tb + L.tk.cs);
-      const int t = t0 + k;
-      const int pos = p.counters[0] + (p.seq_len > 0 ? t % p.seq_len : 0);
+    // ---- phase 0: rows of each token. The 16-byte chunks of every token's projections (and
+    // cx) are loaded in batches of three per thread before any is stored, so the tokens'
+    // loads are in flight together.
+    {
+      const int nproj = 3 * HD / 8, ncx = p.use_moe ? D / 8 : 0, per_tok = nproj + ncx;
+      const int items = ntok * per_tok;
+      constexpr int kBatch = 3;
+      for (int base = 0; base < items; base += kBatch * nthr) {
+        float v[kBatch][8];
+#pragma unroll
+        for (int m = 0; m < kBatch; ++m) {
+          const int it = base + tid + m * nthr;
+          if (it < items) {
+            const int k = it / per_tok, j = it % per_tok, t = t0 + k;
+            const T* src = j < nproj ? reinterpret_cast<const T*>(p.proj) + (size_t)t * 3 * HD + j * 8
+                                     : reinterpret_cast<const T*>(p.rt[2].x) + (size_t)t * p.rt[2].ldx + (j - nproj) * 8;
+            load8(src, v[m]);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < kBatch; ++m) {
+          const int it = base + tid + m * nthr;
+          if (it < items) {
+            const int k = it / per_tok, j = it % per_tok;
+            uint8_t* tb = smb + L.tok0 + k * L.tk.bytes;
+            float* dst;
+            if (j < nproj) {
+              if (j * 8 < HD)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[m][e] = rnd<T>(v[m][e] * p.attn_scale);  // :405
+              dst = reinterpret_cast<float*>(tb + L.tk.row) + j * 8;
+            } else {
+              dst = reinterpret_cast<float*>(tb + L.tk.cxs) + (j - nproj) * 8;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dst[e] = v[m][e];
+          }
+        }
+      }
       // cos / sin (OneRotaryEmbedding, :159-182): fp32 inv_freq * pos, cast to the dtype
-      for (int i = tid; i < half; i += nthr) {
+      for (int it = tid; it < ntok * half; it += nthr) {
+        const int k = it / half, i = it % half, t = t0 + k;
+        float* cs = reinterpret_cast<float*>(smb + L.tok0 + k * L.tk.bytes + L.tk.cs);
+        const int pos = p.counters[0] + (p.seq_len > 0 ? t % p.seq_len : 0);
         const float f = p.inv_freq[i] * (float)pos;
         const float c = rnd<T>(cosf(f)), sn = rnd<T>(sinf(f));
         cs[i] = c; cs[i + half] = c;
         cs[Dh + i] = sn; cs[Dh + i + half] = sn;
       }
-      const T* pr = reinterpret_cast<const T*>(p.proj) + (size_t)t * 3 * HD;
-      for (int i = tid * 8; i < 3 * HD; i += nthr * 8) {
-        float v[8];
-        load8(pr + i, v);
-        if (i < HD)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = rnd<T>(v[e] * p.attn_scale);  // :405
-#pragma unroll
-        for (int e = 0; e < 8; ++e) row[i + e] = v[e];
-      }
-      if (p.use_moe) {
-        float* cxs = reinterpret_cast<float*>(tb + L.tk.cxs);
-        float* gl = reinterpret_cast<float*>(tb + L.tk.gl);
-        const T* X = reinterpret_cast<const T*>(p.rt[2].x) + (size_t)t * p.rt[2].ldx;
-        for (int i = tid * 8; i < D; i += nthr * 8) {
-          float v[8];
-          load8(X + i, v);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) cxs[i + e] = v[e];
+      if (p.use_moe)
+        for (int it = tid; it < ntok * r; it += nthr) {
+          const int k = it / r, j = it % r;
+          float* gl = reinterpret_cast<float*>(smb + L.tok0 + k * L.tk.bytes + L.tk.gl);
+          gl[2 * r + j] = ld<T>(reinterpret_cast<const T*>(p.rt[2].glog) + (size_t)(t0 + k) * r + j);
         }
-        const T* G = reinterpret_cast<const T*>(p.rt[2].glog) + (size_t)t * r;
-        for (int j = tid; j < r; j += nthr) gl[2 * r + j] = ld<T>(G + j);
-      }
     }
     __syncthreads();
 
