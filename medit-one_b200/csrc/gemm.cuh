@@ -267,22 +267,27 @@ struct TcCfg {
   static constexpr int kThreads = 192;  // w0 TMA, w1 MMA + TMEM owner, w2..5 epilogue
 };
 
-// Epilogue of the tensor-core GEMM, run by the 128 threads of warps 2..5 (e = thread - 64).
+// Epilogue of the tensor-core GEMM, run by all six warps (e = 0..191: warps 2..5 first, then
+// the TMA and MMA warps once their loops are done).
 //   prefetch: right after the dependency wait, each thread loads the bias of its 8-row slice
 //             and, for the kinds that read an activation (hx, mean), the aux vectors of its
 //             output units into registers, so no global load sits behind the accumulator.
-//   E1: the TMEM lane quarter (warp % 4) is copied into a shared fp32 tile S[token][row]
-//       (the drained pipeline buffers), kChunk tokens at a time.
+//   E1: warps 2..5 copy their TMEM lane quarter (warp % 4) into a shared fp32 tile
+//       S[token][row] (the drained pipeline buffers), kChunk tokens at a time.
 //   E2: unit = (token, 8 consecutive rows) [GELU_UP: (token, 8 outputs from 16 rows)];
-//       thread e owns the row slice e % 16 (e % 8) of every 8th (16th) token; 16-byte stores.
+//       thread e owns the row slice e % 16 (e % 8) of every 12th (24th) token; 16-byte stores.
 template <int BN>
 __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProblem& P, float* S, uint32_t tmem,
                                             uint64_t* accb, int m_tile, int n_tile, int split) {
   using T = __nv_bfloat16;
   constexpr int CH = TcCfg<BN>::kChunk < 64 ? TcCfg<BN>::kChunk : 64;  // <= 8 prefetched vectors per thread
-  constexpr int KU = CH / 8;   // (token, 8-row) units per thread per chunk
-  constexpr int KG = CH / 16;  // gelu units per thread per chunk
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, e = threadIdx.x - 64, q = warp & 3;
+  constexpr int NT = 192;                 // epilogue threads
+  constexpr int TU = NT / 16, TG = NT / 8; // tokens covered per pass: (token, 8-row) / gelu units
+  constexpr int KU = (CH + TU - 1) / TU;   // (token, 8-row) units per thread per chunk
+  constexpr int KG = (CH + TG - 1) / TG;   // gelu units per thread per chunk
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = warp & 3;
+  const int e = warp >= 2 ? threadIdx.x - 64 : threadIdx.x + 128;
+  const bool drain = warp >= 2;  // owns a TMEM lane quarter
   const int n_base = m_tile * 128;
   const int t_tile = n_tile * BN;
   const int kind = P.kind;
@@ -304,9 +309,9 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
   auto aux_load = [&](int cc) {
 #pragma unroll
     for (int k = 0; k < KU; ++k) {
-      const int t = t_tile + cc + (e >> 4) + 8 * k;
+      const int t = t_tile + cc + (e >> 4) + TU * k;
       auxr[k] = make_uint4(0, 0, 0, 0);
-      if (aux_kind && v8 && t < P.T && (e >> 4) + 8 * k < CH)
+      if (aux_kind && v8 && t < P.T && (e >> 4) + TU * k < CH)
         auxr[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0);
     }
   };
@@ -326,7 +331,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
       const int nrow = n_base + q * 32 + lane;
       const int nl = q * 32 + lane;
       T* out = reinterpret_cast<T*>(P.out);
-      if (ok)
+      if (ok && drain)
         for (int c0 = 0; c0 < CH; c0 += 16) {
           if (c0 >= tn) break;  // warp-uniform
           float v[16];
@@ -345,8 +350,8 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
             if (lane == 0) K[q * CH + c0 + j] = key;
           }
         }
-      named_barrier_sync(1, 128);
-      for (int tl = e; tl < tn; tl += 128) {
+      named_barrier_sync(1, NT);
+      for (int tl = e; tl < tn; tl += NT) {
         uint32_t best = 0u;
 #pragma unroll
         for (int w = 0; w < 4; ++w) best = max(best, K[w * CH + tl]);
@@ -357,10 +362,10 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
                     ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n));
         }
       }
-      named_barrier_sync(1, 128);
+      named_barrier_sync(1, NT);
       continue;
     }
-    if (ok)
+    if (ok && drain)
       for (int c0 = 0; c0 < CH; c0 += 16) {
         if (c0 >= tn) break;  // warp-uniform
         float v[16];
@@ -369,7 +374,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
 #pragma unroll
         for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
       }
-    named_barrier_sync(1, 128);
+    named_barrier_sync(1, NT);
     // ---- E2
     const int tb = t_tile + cc;
     if (false) {
@@ -377,7 +382,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
       T* out = reinterpret_cast<T*>(P.out);
 #pragma unroll
       for (int k = 0; k < KG; ++k) {
-        const int tl = (e >> 3) + 16 * k;
+        const int tl = (e >> 3) + TG * k;
         if (tl >= tn || ng >= P.Nw) continue;
         const float* sv = S + tl * 128 + cg * 16;
         float o8[8];
@@ -392,7 +397,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
     } else {
 #pragma unroll
       for (int k = 0; k < KU; ++k) {
-        const int tl = (e >> 4) + 8 * k;
+        const int tl = (e >> 4) + TU * k;
         if (tl >= tn || !v8) continue;
         const int t = tb + tl;
         float a[8];
@@ -437,7 +442,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
         }
       }
     }
-    named_barrier_sync(1, 128);
+    named_barrier_sync(1, NT);
   }
 }
 
@@ -532,8 +537,9 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
       umma_commit(accb);
     }
   }
-  // ---------------- epilogue (warps 2..5 only; warps 0..1 go straight to teardown)
-  if (warp >= 2) tc_epilogue<BN>(p, P, reinterpret_cast<float*>(smem), tmem, accb, m_tile, n_tile, split);
+  // ---------------- epilogue (all six warps; the TMA / MMA lanes rejoin their warps first)
+  __syncwarp();
+  tc_epilogue<BN>(p, P, reinterpret_cast<float*>(smem), tmem, accb, m_tile, n_tile, split);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
