@@ -135,6 +135,18 @@ ONE_DEVINL void chunk_norm(const float* x, float ss, int D, float eps, const T* 
   }
 }
 
+// chunk_norm with the weight / bias chunk already in registers (bv unused when has_b is false)
+template <typename T>
+ONE_DEVINL void chunk_norm_r(const float* x, float ss, int D, float eps, const float* wv, const float* bv, bool has_b,
+                             float* y) {
+  const float r = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float v = rnd<T>(wv[e] * rnd<T>(x[e] * r));
+    y[e] = has_b ? rnd<T>(v + bv[e]) : v;
+  }
+}
+
 ONE_DEVINL float sumsq8(const float* x) {
   float s = 0.f;
 #pragma unroll
@@ -147,14 +159,26 @@ ONE_DEVINL float sumsq8(const float* x) {
 template <typename T>
 __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
   __shared__ float red[4 * 32];
-  pdl_launch_dependents();
-  pdl_wait();
   const int t = blockIdx.x;
   const int c = threadIdx.x;
   const int D = p.D;
   const bool act = c < D / 8;
   const size_t off = (size_t)t * D + (size_t)c * 8;
   float h[8], a[8], b[8];
+  // weights (not written by any kernel of the step): before the dependency wait
+  float w1[8], pw[8], pb[8], db[8];
+  const bool mid = p.mode != PRE_FIRST;
+  if (act) {
+    // norm1 is absent in PRE_FINAL (the kernel returns before norm_x there)
+    if (p.norm1_w) load8(reinterpret_cast<const T*>(p.norm1_w) + c * 8, w1);
+    if (mid && p.prev_norm_w) {
+      load8(reinterpret_cast<const T*>(p.prev_norm_w) + c * 8, pw);
+      if (p.prev_norm_b) load8(reinterpret_cast<const T*>(p.prev_norm_b) + c * 8, pb);
+      if (p.down_b) load8(reinterpret_cast<const T*>(p.down_b) + c * 8, db);
+    }
+  }
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (p.mode == PRE_FIRST) {
     __shared__ int sid;
@@ -189,28 +213,35 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
       store8(reinterpret_cast<T*>(p.cx) + off, h);
       store8(reinterpret_cast<T*>(p.cxc) + off, b);
     }
-  } else {
+  }
+  // the running-sum row of this layer (read-modify-write below), requested early
+  float sr[8];
+  if (p.decode && act && p.mode != PRE_FINAL) load8(p.S + off, sr);
+  if (mid) {
     // finish the previous layer: out = norm(out0 + down_proj(...)) (:571-573), h += out (:793),
-    // hx = norm(hx + hx_moe) (:563-564)
+    // hx = norm(hx + hx_moe) (:563-564). The split-K partials are loaded eight at a time
+    // before they are added, in split order.
     float hp[8];
     if (act) {
       float m[8];
       load8(reinterpret_cast<const T*>(p.out0) + off, a);
       load8(reinterpret_cast<const T*>(p.h) + off, h);
       load8(reinterpret_cast<const T*>(p.hx_pre) + off, hp);
-      load8(p.ws + off, m);
-      for (int s = 1; s < p.splits; ++s) {
-        float v[8];
-        load8(p.ws + (size_t)s * p.T * D + off, v);
+      for (int s0 = 0; s0 < p.splits; s0 += 8) {
+        float v[8][8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) m[e] += v[e];
-      }
-      if (p.down_b) {
-        float v[8];
-        load8(reinterpret_cast<const T*>(p.down_b) + c * 8, v);
+        for (int j = 0; j < 8; ++j)
+          if (s0 + j < p.splits) load8(p.ws + (size_t)(s0 + j) * p.T * D + off, v[j]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) m[e] += v[e];
+        for (int j = 0; j < 8; ++j)
+          if (s0 + j < p.splits) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) m[e] = (s0 + j == 0) ? v[j][e] : m[e] + v[j][e];
+          }
       }
+      if (p.down_b)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m[e] += db[e];
 #pragma unroll
       for (int e = 0; e < 8; ++e) a[e] = rnd<T>(a[e] + rnd<T>(m[e]));
     } else {
@@ -219,13 +250,11 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
     }
     float ss[2] = {sumsq8(a), sumsq8(hp)};
     block_sum<2>(ss, red, 0);
-    const T* nw = reinterpret_cast<const T*>(p.prev_norm_w);
-    const T* nb = reinterpret_cast<const T*>(p.prev_norm_b);
     if (act) {
-      chunk_norm<T>(a, ss[0], D, 1e-6f, nw, nb, c, b);
+      chunk_norm_r<T>(a, ss[0], D, 1e-6f, pw, pb, p.prev_norm_b != nullptr, b);
 #pragma unroll
       for (int e = 0; e < 8; ++e) h[e] = rnd<T>(h[e] + b[e]);
-      chunk_norm<T>(hp, ss[1], D, 1e-6f, nw, nb, c, b);
+      chunk_norm_r<T>(hp, ss[1], D, 1e-6f, pw, pb, p.prev_norm_b != nullptr, b);
       store8(reinterpret_cast<T*>(p.hx) + off, b);
       store8(reinterpret_cast<T*>(p.h) + off, h);
     }
@@ -241,12 +270,10 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
   }
   if (p.mode == PRE_FIRST && act) store8(reinterpret_cast<T*>(p.h) + off, h);
   // norm_x = norm1(h) (:340); OneRMSNorm(dim) keeps eps = 1e-6 and has no bias
-  float sr[8];
-  if (p.decode && act) load8(p.S + off, sr);
   float s3[1] = {act ? sumsq8(h) : 0.f};
   block_sum<1>(s3, red, 3);
   if (!act) return;
-  chunk_norm<T>(h, s3[0], D, 1e-6f, reinterpret_cast<const T*>(p.norm1_w), (const T*)nullptr, c, a);
+  chunk_norm_r<T>(h, s3[0], D, 1e-6f, w1, w1, false, a);
   store8(reinterpret_cast<T*>(p.norm_x) + off, a);
   if (p.decode) {
     // running sum replaces cache.update + cumsum (:358-376); mean = sum / arange[-1] (:379-387)

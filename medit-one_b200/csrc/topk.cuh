@@ -126,10 +126,8 @@ template <class Q>
 ONE_HDINL void tk_heap_select(Q& q, int first, int middle, int last) {
   const int len = middle - first;
   if (len >= 2)
-    for (int parent = (len - 2) / 2;; --parent) {
+    for (int parent = (len - 2) / 2; parent >= 0; --parent)
       tk_adjust_heap(q, first, parent, len, q.gv(first + parent), q.gi(first + parent));
-      if (parent == 0) break;
-    }
   for (int i = middle; i < last; ++i)
     if (tk_gt(q.gv(i), q.gv(first))) {
       const float v = q.gv(i);
@@ -206,6 +204,8 @@ ONE_HDINL void topk_select(const float* score, int n, int k, int* out) {
 // The selection topk_select makes on n equal scores, packed one index per byte (k <= 8):
 // it depends only on (n, k), so hosts compute it once and pass it to the kernels.
 inline unsigned long long topk_tie_selection(int n, int k) {
+  n = n < 1 ? 1 : (n > kMaxExperts ? kMaxExperts : n);
+  k = k < 1 ? 1 : (k > n ? n : k);
   float z[kMaxExperts];
   int out[kMaxExperts];
   for (int j = 0; j < n; ++j) z[j] = 0.f;
