@@ -488,13 +488,6 @@ def prefill_cpu(cfg, seqs: int, length: int) -> dict:
                                      f"forward, bf16)"}
 
 
-def prefill_launches(cfg) -> int:
-    """Kernels of one prefill call: per layer row_pre, prefix-mean scan, GEMM A, attention/routers,
-    GEMM C, gate/up, down; then row_pre, up_scaler, row_norm, lm_head (+argmax of each prompt's
-    last position), the counter update."""
-    return cfg.num_hidden_layers * 7 + 5
-
-
 def run_prefill(args, ws, rank, local):
     """One step = prefill of 64 prompts of 4096 tokens (the per-GPU share of the 4096 x 4096 prompt
     set is 512 prompts: 8 steps); then the decode rate at batch 64 from that state."""
@@ -570,7 +563,7 @@ def run_prefill(args, ws, rank, local):
                              "frac": fl / t_step / 1e12 / tf_sus, "peak_source": src + " (sustained)",
                              "traffic": None, "flops_per_token": gemm_flops_per_token(cfg)},
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": tokens * 8, "d2h_bytes_per_step": PF_B * 4},
-                "gpu_launches": args.steps * prefill_launches(cfg), "clocks": clocks}
+                "gpu_launches": args.steps * eng.prefill_launches(PF_B, PF_S), "clocks": clocks}
         if ws == 1 and not args.no_cpu_baseline:
             r = prefill_cpu(cfg, 8, 1024)
             line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}

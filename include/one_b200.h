@@ -122,6 +122,9 @@ void* one_engine_buffer(one_engine* e, const char* name);
 int one_engine_error(one_engine* e, int32_t* code, int32_t* where);
 /* Number of kernels one_engine_step launches for `batch` sequences. */
 int32_t one_engine_step_launches(one_engine* e, int32_t batch);
+/* Number of kernels one_engine_prefill launches for `batch` prompts of `seq_len` tokens
+ * (logits_mode as in one_engine_prefill), or -1. */
+int32_t one_engine_prefill_launches(one_engine* e, int32_t batch, int32_t seq_len, int32_t logits_mode);
 /* Time each launch of one decode step separately (reps back-to-back runs between two
  * CUDA events on `stream`, warm caches): us_out[i] = mean microseconds of launch i.
  * Returns the number of launches written (<= n), or -1. Advances the decode state. */

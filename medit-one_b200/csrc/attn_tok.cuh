@@ -1,0 +1,284 @@
+// Prompt-ingestion feature attention, one warp per token (bf16 models, H <= 16 heads,
+// even H, head_dim 32 or 64).
+//
+// The decode kernel (row_attn_kernel) is shaped for the latency of 256 tokens; a prompt
+// call has 10^5..10^6 tokens, so here every warp takes whole tokens with no CTA-wide
+// barrier after the weights are staged, and the routers run afterwards as separate
+// launches (gate GEMM on the tensor cores, moe_router_kernel).
+//
+// Per token (one/modeling_one.py:390-556): q = single_x * scale, RoPE (rotate_half) on q and
+// on the key, the three head projections lin_q / lin_k / lin_v (Dh -> H) as one m16n8k16
+// mma.sync chain with the heads as the M rows, bias, logits q * k, softmax over the H
+// outputs of each head (fp32, rounded), o = w * v. Every elementwise step that the
+// reference rounds to bf16 is computed on packed bf16x2 operands with an explicit
+// round-to-nearest instruction: for bf16 inputs the fp32 product of two values is exact
+// and an fp32 sum that is inexact lies far from any bf16 rounding boundary, so one
+// rounding of the exact result equals the reference's fp32-then-bf16 rounding.
+#pragma once
+
+#include "common.cuh"
+#include "rows.cuh"
+
+namespace one {
+
+constexpr int kTokWarps = 8;
+
+struct AttnTokParams {
+  int T, H, seq_len;
+  const __nv_bfloat16* rope;  // [seq_len][Dh]: cos(f_i) for i < Dh/2, then sin(f_i); f_i = inv_freq_i * (pos0 + s)
+  const __nv_bfloat16* proj;  // [T][3 * H * Dh]: lin1 | lin2 | lin3 outputs (bias added)
+  float scale;                // attention scale 1/sqrt(Dh)
+  uint32_t scale2;            // the scale as bf16x2, when scale_exact (a bf16 value)
+  int scale_exact;
+  const __nv_bfloat16 *wq, *bq, *wk, *bk, *wv, *bv;  // lin_q / lin_k / lin_v [H, Dh], [H]
+  __nv_bfloat16* out;         // [T][H * H]
+  uint32_t clamp2;            // bf16x2 bound of the LinearMoE input clamp (0: store o unclamped)
+};
+
+// RoPE table of one prompt call (OneRotaryEmbedding, one/modeling_one.py:159-182): the fp32
+// angle inv_freq_i * pos, cos / sin rounded to bf16. Shared by all layers of the call.
+struct RopeTabParams {
+  const int* counters;  // counters[0] = position of the first prompt token
+  const float* inv_freq;
+  int seq_len, half;
+  __nv_bfloat16* tab;   // [seq_len][2 * half]
+};
+
+__global__ void rope_table_kernel(const RopeTabParams p) {
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= p.seq_len * p.half) return;
+  const int s = i / p.half, j = i % p.half;
+  const float f = p.inv_freq[j] * (float)(p.counters[0] + s);
+  p.tab[(size_t)s * 2 * p.half + j] = __float2bfloat16_rn(cosf(f));
+  p.tab[(size_t)s * 2 * p.half + p.half + j] = __float2bfloat16_rn(sinf(f));
+}
+
+// packed bf16x2 arithmetic, each result rounded once to nearest-even
+ONE_DEVINL uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_min(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL float bf2_lo(uint32_t u) { return __uint_as_float(u << 16); }
+ONE_DEVINL float bf2_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// Shared memory (bytes): lin_q / lin_k / lin_v as [3][16][RS] bf16 (rows >= H zero), biases
+// [3][16] fp32, then per warp the token's q | k | v rows [3H][RS] bf16 and the output row
+// [H*H] bf16. RS = Dh + 16: a row stride of 8 (mod 32) words makes the warp's 8-byte
+// fragment loads (8 rows x 4 column groups) conflict-free.
+template <int DH>
+struct AttnTokSmem {
+  static constexpr int RS = DH + 16;
+  static constexpr int W = 0;
+  static constexpr int BIAS = 3 * 16 * RS * 2;
+  static constexpr int WARP0 = BIAS + 3 * 16 * 4;
+  __host__ __device__ static int per_warp(int H) { return (3 * H * RS * 2 + H * H * 2 + 15) & ~15; }
+  __host__ __device__ static int total(int H) { return WARP0 + kTokWarps * per_warp(H); }
+};
+
+// Fragment layout of the projections: m16n8k16 with rows = heads g and g + 8, columns =
+// outputs. Within each 16-wide k slice, lane (g, c) supplies the logical k = 4c..4c+3 (one
+// 8-byte load) as the hardware's k = {2c, 2c+1, 2c+8, 2c+9}; A and B use the same
+// assignment, so every product pairs the same (k) elements.
+template <int DH>
+__global__ void __launch_bounds__(kTokWarps * 32, 2) attn_tok_kernel(const AttnTokParams p) {
+  using S = AttnTokSmem<DH>;
+  constexpr int RS = S::RS, NS = DH / 16, HALF = DH / 2, NCH = DH / 8;
+  constexpr int kMaxLd = (3 * 16 * NCH + 31) / 32;
+  extern __shared__ __align__(16) uint8_t smb[];
+  const int H = p.H, HD = H * DH, HH = H * H;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(smb + S::W);
+  float* bs = reinterpret_cast<float*>(smb + S::BIAS);
+
+  // weights (never written by the preceding kernels): staged before the dependency wait
+  for (int v = tid; v < 3 * 16 * NCH; v += blockDim.x) {
+    const int row = v / NCH, ch = v % NCH, pj = row / 16, n = row % 16;
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    if (n < H) {
+      const __nv_bfloat16* W = pj == 0 ? p.wq : pj == 1 ? p.wk : p.wv;
+      val = *reinterpret_cast<const uint4*>(W + (size_t)n * DH + ch * 8);
+    }
+    *reinterpret_cast<uint4*>(ws + row * RS + ch * 8) = val;
+  }
+  for (int i = tid; i < 3 * 16; i += blockDim.x) {
+    const int pj = i / 16, n = i % 16;
+    const __nv_bfloat16* B = pj == 0 ? p.bq : pj == 1 ? p.bk : p.bv;
+    bs[i] = n < H ? __bfloat162float(B[n]) : 0.f;
+  }
+  __syncthreads();
+  pdl_wait();
+
+  uint8_t* wb = smb + S::WARP0 + warp * S::per_warp(H);
+  __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(wb);
+  uint32_t* stage = reinterpret_cast<uint32_t*>(wb + 3 * H * RS * 2);
+  const int nch = 3 * H * NCH;  // 16-byte chunks of one token's q | k | v row
+  const bool two_nt = H > 8;
+  const uint32_t negc = p.clamp2 ^ 0x80008000u;
+  for (int t = blockIdx.x * kTokWarps + warp; t < p.T; t += gridDim.x * kTokWarps) {
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(p.proj + (size_t)t * 3 * HD);
+      uint4 v[kMaxLd];
+#pragma unroll
+      for (int m = 0; m < kMaxLd; ++m) {
+        const int j = lane + 32 * m;
+        if (j < nch) v[m] = src[j];
+      }
+#pragma unroll
+      for (int m = 0; m < kMaxLd; ++m) {
+        const int j = lane + 32 * m;
+        if (j < nch) *reinterpret_cast<uint4*>(rows + (j / NCH) * RS + (j % NCH) * 8) = v[m];
+      }
+    }
+    const __nv_bfloat16* tab = p.rope + (size_t)(t % p.seq_len) * DH;
+    uint2 cs[NS / 2], sn[NS / 2];
+#pragma unroll
+    for (int ls = 0; ls < NS / 2; ++ls) {
+      cs[ls] = *reinterpret_cast<const uint2*>(tab + ls * 16 + 4 * c);
+      sn[ls] = *reinterpret_cast<const uint2*>(tab + HALF + ls * 16 + 4 * c);
+    }
+    __syncwarp();
+
+    float acc[3][2][4];
+#pragma unroll
+    for (int pj = 0; pj < 3; ++pj)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[pj][nt][q] = 0.f;
+#pragma unroll
+    for (int pj = 0; pj < 3; ++pj) {
+      uint32_t a[NS][4];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int h = g + 8 * rr;
+        const bool ok = h < H;
+        const __nv_bfloat16* rw = rows + (pj * H + (ok ? h : 0)) * RS + 4 * c;
+#pragma unroll
+        for (int ls = 0; ls < NS / 2; ++ls) {
+          uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
+          if (ok) {
+            lo = *reinterpret_cast<const uint2*>(rw + ls * 16);
+            hi = *reinterpret_cast<const uint2*>(rw + (ls + NS / 2) * 16);
+          }
+          if (pj < 2) {
+            if (pj == 0) {  // single_x * scale (:405)
+              if (p.scale_exact) {
+                lo = make_uint2(bf2_mul(lo.x, p.scale2), bf2_mul(lo.y, p.scale2));
+                hi = make_uint2(bf2_mul(hi.x, p.scale2), bf2_mul(hi.y, p.scale2));
+              } else {
+                const float sc = p.scale;
+                lo = make_uint2(pack_bf16x2(bf2_lo(lo.x) * sc, bf2_hi(lo.x) * sc),
+                                pack_bf16x2(bf2_lo(lo.y) * sc, bf2_hi(lo.y) * sc));
+                hi = make_uint2(pack_bf16x2(bf2_lo(hi.x) * sc, bf2_hi(hi.x) * sc),
+                                pack_bf16x2(bf2_lo(hi.y) * sc, bf2_hi(hi.y) * sc));
+              }
+            }
+            // x * cos + rotate_half(x) * sin: out[d] = x[d] cos - x[d + half] sin,
+            // out[d + half] = x[d + half] cos + x[d] sin (cos / sin of index d)
+            const uint2 rl = make_uint2(bf2_sub(bf2_mul(lo.x, cs[ls].x), bf2_mul(hi.x, sn[ls].x)),
+                                        bf2_sub(bf2_mul(lo.y, cs[ls].y), bf2_mul(hi.y, sn[ls].y)));
+            const uint2 rh = make_uint2(bf2_add(bf2_mul(hi.x, cs[ls].x), bf2_mul(lo.x, sn[ls].x)),
+                                        bf2_add(bf2_mul(hi.y, cs[ls].y), bf2_mul(lo.y, sn[ls].y)));
+            lo = rl;
+            hi = rh;
+          }
+          a[ls][rr] = lo.x;
+          a[ls][rr + 2] = lo.y;
+          a[ls + NS / 2][rr] = hi.x;
+          a[ls + NS / 2][rr + 2] = hi.y;
+        }
+      }
+      const __nv_bfloat16* wrow = ws + pj * 16 * RS + 4 * c;
+#pragma unroll
+      for (int ks = 0; ks < NS; ++ks)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          if (nt == 0 || two_nt) {
+            const uint2 b = *reinterpret_cast<const uint2*>(wrow + (nt * 8 + g) * RS + ks * 16);
+            mma_16816_bf16(acc[pj][nt], a[ks], b.x, b.y);
+          }
+    }
+
+    // lane (g, c): heads h = g + 8 rr, outputs j = 8 nt + 2c + {0, 1}
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int h = g + 8 * rr;
+      uint32_t lg[2], vv[2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int j = nt * 8 + 2 * c;
+        const uint32_t q2 = pack_bf16x2(acc[0][nt][2 * rr] + bs[j], acc[0][nt][2 * rr + 1] + bs[j + 1]);
+        const uint32_t k2 = pack_bf16x2(acc[1][nt][2 * rr] + bs[16 + j], acc[1][nt][2 * rr + 1] + bs[16 + j + 1]);
+        vv[nt] = pack_bf16x2(acc[2][nt][2 * rr] + bs[32 + j], acc[2][nt][2 * rr + 1] + bs[32 + j + 1]);
+        const uint32_t m = (j < H ? 0u : 0xffffu) | (j + 1 < H ? 0u : 0xffff0000u);
+        lg[nt] = (bf2_mul(q2, k2) & ~m) | (0xff80ff80u & m);  // masked outputs: -inf
+      }
+      uint32_t m2 = bf2_max(lg[0], lg[1]);
+      float mx = fmaxf(bf2_lo(m2), bf2_hi(m2));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const uint32_t mx2 = pack_bf16x2(mx, mx);
+      uint32_t d1[2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) d1[nt] = bf2_sub(lg[nt], mx2);
+      m2 = bf2_max(d1[0], d1[1]);
+      float mm = fmaxf(bf2_lo(m2), bf2_hi(m2));
+      mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
+      mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
+      float ex[4], sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int nt = q >> 1, j = nt * 8 + 2 * c + (q & 1);
+        const float d = (q & 1) ? bf2_hi(d1[nt]) : bf2_lo(d1[nt]);
+        ex[q] = j < H ? expf(d - mm) : 0.f;
+        sum += ex[q];
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      const float inv = 1.0f / sum;
+      if (h < H) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int j = nt * 8 + 2 * c;
+          if (j < H) {
+            float w0 = ex[2 * nt] * inv, w1 = ex[2 * nt + 1] * inv;
+            if (isnan(w0)) w0 = 1.0f / (float)H;
+            if (isnan(w1)) w1 = 1.0f / (float)H;
+            uint32_t o2 = bf2_mul(pack_bf16x2(w0, w1), vv[nt]);
+            if (p.clamp2) o2 = bf2_min(bf2_max(o2, negc), p.clamp2);  // LinearMoE clamp (one/linear_moe.py:53)
+            stage[(h * H + j) >> 1] = o2;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (size_t)t * HH);
+    for (int w = lane; w < HH / 2; w += 32) dst[w] = stage[w];
+    __syncwarp();
+  }
+}
+
+}  // namespace one

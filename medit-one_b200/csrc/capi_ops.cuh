@@ -17,23 +17,9 @@ extern "C" size_t one_linear_moe_workspace_bytes(int32_t n, int32_t fin, int32_t
 }
 
 static int router_launch(const MoeRouter& R, int n, int r, int E, int k, int dtype, cudaStream_t st) {
-  const int es = dtype == ONE_DTYPE_F32 ? 4 : 2;
-  const size_t smem = moe_router_smem_bytes(R.in, r, E, es);
-  const int warps = moe_router_warps(R.in, r, E, es);
-  if (warps < 1 || smem > 220 * 1024) return fail(ONE_ERR_UNSUPPORTED, "router: %zu B of shared memory", smem);
-  const int per_sm = std::max(1, std::min(2048 / (32 * warps), (int)((228 * 1024) / (smem + 1024))));
-  // tokens per warp group: enough groups for ~24 warps per SM; the selections of a group run
-  // one per lane
-  const int group = std::max(1, std::min(32, n / (num_sms() * 24)));
-  const int groups = (n + group - 1) / group;
-  const int grid = std::max(1, std::min((groups + warps - 1) / warps, num_sms() * per_sm));
-  cudaError_t e = dtype == ONE_DTYPE_BF16
-                      ? launch_k(moe_router_kernel<__nv_bfloat16>, dim3(grid), dim3(32 * warps), smem, st, R, n, r,
-                                 E, k, group, topk_tie_selection(E, std::min(k, E)))
-                      : launch_k(moe_router_kernel<float>, dim3(grid), dim3(32 * warps), smem, st, R, n, r, E, k,
-                                 group, topk_tie_selection(E, std::min(k, E)));
-  if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "router launch: %s", cudaGetErrorString(e));
-  return ONE_OK;
+  Launch L;
+  const int rc = plan_router(L, R, n, r, E, k, dtype);
+  return rc ? rc : run(L, st);
 }
 
 extern "C" int one_linear_moe(const void* x, int32_t n, int32_t fin, int32_t fout, const void* weight, const void* bias,

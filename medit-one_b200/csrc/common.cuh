@@ -73,6 +73,14 @@ ONE_DEVINL double warp_sum_d(double v) {
   return v;
 }
 
+// x.clamp(-1e4, 1e4) of a LinearMoE input (one/linear_moe.py:53) kept in fp32: the bound is 1e4
+// converted to the tensor's type, 9984 for bf16
+template <typename T>
+ONE_DEVINL float moe_clamp(float v) {
+  const float b = rnd<T>(1e4f);
+  return fminf(fmaxf(v, -b), b);
+}
+
 // exact (erf) GELU as computed by torch on fp32: x * 0.5 * (1 + erf(x / sqrt(2)))
 ONE_DEVINL float gelu_erf(float x) { return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f)); }
 // SiLU as computed by torch on fp32: x / (1 + exp(-x))

@@ -31,6 +31,7 @@
 #include "ops.cuh"
 #include "rows.cuh"
 #include "flash_attn.cuh"
+#include "attn_tok.cuh"
 
 using namespace one;
 
@@ -111,7 +112,10 @@ struct ProbSpec {
   int max_splits = 1;
 };
 
-enum LaunchKind { L_GEMM_TC, L_GEMM_SIMT, L_ROW_PRE, L_ROW_ATTN, L_SCAN, L_ROW_NORM, L_ADVANCE, L_NEXT_IDS };
+enum LaunchKind {
+  L_GEMM_TC, L_GEMM_SIMT, L_ROW_PRE, L_ROW_ATTN, L_SCAN, L_ROW_NORM, L_ADVANCE, L_NEXT_IDS,
+  L_ROPE_TAB, L_ATTN_TOK, L_ROUTER
+};
 
 struct AdvanceParams {
   int* counters;
@@ -164,6 +168,13 @@ struct Launch {
   RowNormParams rn;
   AdvanceParams ad;
   NextIdsParams ni;
+  RopeTabParams rt;
+  AttnTokParams at;
+  struct {
+    MoeRouter R;
+    int n, r, E, k, group;
+    unsigned long long tie;
+  } ro;
 };
 
 static int g_num_sms = 0;
@@ -313,6 +324,8 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(moe_router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(moe_router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem));
+  CK(cudaFuncSetAttribute(attn_tok_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<32>::total(16)));
+  CK(cudaFuncSetAttribute(attn_tok_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<64>::total(16)));
   g_attrs_set = true;
   return ONE_OK;
 }
@@ -363,6 +376,19 @@ static int run(const Launch& L, cudaStream_t st) {
       e = bf ? launch_k(scan_mean_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), 0, st, L.sc)
              : launch_k(scan_mean_kernel<float>, dim3(L.grid), dim3(L.block), 0, st, L.sc);
       break;
+    case L_ROPE_TAB: e = launch_k(rope_table_kernel, dim3(L.grid), dim3(L.block), 0, st, L.rt); break;
+    case L_ATTN_TOK:
+      switch (L.nv) {
+        case 32: e = launch_k(attn_tok_kernel<32>, dim3(L.grid), dim3(L.block), L.smem, st, L.at); break;
+        default: e = launch_k(attn_tok_kernel<64>, dim3(L.grid), dim3(L.block), L.smem, st, L.at); break;
+      }
+      break;
+    case L_ROUTER:
+      e = bf ? launch_k(moe_router_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), L.smem, st, L.ro.R, L.ro.n,
+                        L.ro.r, L.ro.E, L.ro.k, L.ro.group, L.ro.tie)
+             : launch_k(moe_router_kernel<float>, dim3(L.grid), dim3(L.block), L.smem, st, L.ro.R, L.ro.n, L.ro.r,
+                        L.ro.E, L.ro.k, L.ro.group, L.ro.tie);
+      break;
     case L_ADVANCE: e = launch_k(advance_kernel, dim3(1), dim3(32), 0, st, L.ad); break;
     case L_NEXT_IDS: e = launch_k(next_ids_kernel, dim3(L.grid), dim3(L.block), 0, st, L.ni); break;
   }
@@ -371,6 +397,39 @@ static int run(const Launch& L, cudaStream_t st) {
 }
 
 static int run_plan(const std::vector<Launch>& plan, cudaStream_t st);
+
+// LinearMoE router launch over n tokens with precomputed gate logits (moe_router_kernel).
+static int plan_router(Launch& L, const MoeRouter& R, int n, int r, int E, int k, int dtype) {
+  const int es = dtype == ONE_DTYPE_F32 ? 4 : 2;
+  const size_t smem = moe_router_smem_bytes(R.in, r, E, es);
+  const int warps = moe_router_warps(R.in, r, E, es);
+  if (warps < 1 || smem > 220 * 1024) return fail(ONE_ERR_UNSUPPORTED, "router: %zu B of shared memory", smem);
+  const int per_sm = std::max(1, std::min(2048 / (32 * warps), (int)((228 * 1024) / (smem + 1024))));
+  // tokens per warp group: enough groups for ~24 warps per SM; the selections of a group run
+  // one per lane
+  const int group = std::max(1, std::min(32, n / (num_sms() * 24)));
+  const int groups = (n + group - 1) / group;
+  L.kind = L_ROUTER;
+  L.dtype = dtype;
+  L.smem = smem;
+  L.block = 32 * warps;
+  L.grid = std::max(1, std::min((groups + warps - 1) / warps, num_sms() * per_sm));
+  L.ro.R = R;
+  L.ro.n = n;
+  L.ro.r = r;
+  L.ro.E = E;
+  L.ro.k = k;
+  L.ro.group = group;
+  L.ro.tie = topk_tie_selection(E, std::min(k, E));
+  return ONE_OK;
+}
+
+// Prompt ingestion takes the warp-per-token attention kernel (attn_tok_kernel) for bf16
+// models with an even number of heads <= 16 and head_dim 32 or 64.
+static bool attn_tok_eligible(const one_config& c) {
+  const int H = c.num_attention_heads, Dh = c.head_dim;
+  return c.dtype == ONE_DTYPE_BF16 && H >= 2 && H <= 16 && H % 2 == 0 && (Dh == 32 || Dh == 64);
+}
 
 // ------------------------------------------------------------------ workspace layout
 struct Layout {
@@ -399,6 +458,8 @@ struct Bufs {
   size_t counters; // i32 [4]
   size_t err;      // DevErr
   size_t ridx;     // i32 [Tm, 3, k]
+  size_t ghx, gx;  // [Tm, r] hx_moe / x_moe gate logits (prompt ingestion)
+  size_t rope;     // bf16 [Tm, head_dim] RoPE cos | sin table of a prompt call
   size_t total;
   int ws_rows;
 };
@@ -441,6 +502,9 @@ static Bufs layout(const one_config& c, int max_tokens, int max_batch, int hist_
   b.counters = Lo.take(16);
   b.err = Lo.take(sizeof(DevErr));
   b.ridx = Lo.take(Tm * 3 * (size_t)std::max(c.top_k, 1) * 4);
+  b.ghx = Lo.take(Tm * (size_t)std::max(c.r, 1) * es);
+  b.gx = Lo.take(Tm * (size_t)std::max(c.r, 1) * es);
+  b.rope = Lo.take(Tm * (size_t)c.head_dim * 2);
   b.total = Lo.take(0) + 1024;
   return b;
 }
@@ -609,6 +673,15 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
   auto B_ = [&](size_t off) { return e->at<void>(off); };
   const int* counters = e->at<int>(e->b.counters);
   const int es = es_of(c);
+  const bool tok = !decode && attn_tok_eligible(c);
+  if (tok) {  // RoPE table of the call's positions, shared by every layer
+    Launch rt;
+    rt.kind = L_ROPE_TAB;
+    rt.block = 256;
+    rt.grid = (seq_len * (Dh / 2) + 255) / 256;
+    rt.rt = RopeTabParams{counters, e->inv_freq, seq_len, Dh / 2, e->at<__nv_bfloat16>(e->b.rope)};
+    plan.push_back(rt);
+  }
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const int cur = l & 1, nxt = cur ^ 1;
     // ---- row_pre
@@ -683,8 +756,69 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       if (rc) return rc;
       plan.push_back(g);
     }
-    // ---- attention + routers
-    {
+    // ---- attention + routers, prompt ingestion: warp-per-token attention writes o (the
+    // LinearMoE-clamped copy when routed), then the hx_moe / x_moe gate logits on the tensor
+    // cores and one router launch per LinearMoE
+    if (tok) {
+      Launch a;
+      a.kind = L_ATTN_TOK;
+      a.dtype = dt;
+      a.nv = Dh;
+      a.block = kTokWarps * 32;
+      AttnTokParams& q = a.at;
+      memset(&q, 0, sizeof(q));
+      q.T = T; q.H = H; q.seq_len = seq_len;
+      q.rope = e->at<__nv_bfloat16>(e->b.rope);
+      q.proj = e->at<__nv_bfloat16>(e->b.proj);
+      q.scale = 1.0f / sqrtf((float)Dh);
+      const __nv_bfloat16 sb = __float2bfloat16_rn(q.scale);
+      q.scale_exact = __bfloat162float(sb) == q.scale ? 1 : 0;
+      uint16_t sbits;
+      memcpy(&sbits, &sb, 2);
+      q.scale2 = (uint32_t)sbits * 0x10001u;
+      q.wq = (const __nv_bfloat16*)LW(ONE_W_LINQ_W); q.bq = (const __nv_bfloat16*)LW(ONE_W_LINQ_B);
+      q.wk = (const __nv_bfloat16*)LW(ONE_W_LINK_W); q.bk = (const __nv_bfloat16*)LW(ONE_W_LINK_B);
+      q.wv = (const __nv_bfloat16*)LW(ONE_W_LINV_W); q.bv = (const __nv_bfloat16*)LW(ONE_W_LINV_B);
+      q.out = e->at<__nv_bfloat16>(e->b.o);
+      // bf16(1e4) = 9984: the clamp bound of a bf16 tensor
+      q.clamp2 = moe ? 0x461c461cu : 0u;
+      a.smem = Dh == 32 ? AttnTokSmem<32>::total(H) : AttnTokSmem<64>::total(H);
+      int per_sm = 1;
+      cudaError_t oe = Dh == 32 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_tok_kernel<32>, a.block, a.smem)
+                                : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_tok_kernel<64>, a.block, a.smem);
+      if (oe != cudaSuccess || per_sm < 1) return fail(ONE_ERR_CUDA, "attention kernel does not fit an SM");
+      a.grid = std::max(1, std::min((T + kTokWarps - 1) / kTokWarps, num_sms() * per_sm));
+      plan.push_back(a);
+      if (moe) {
+        ProbSpec ps[2];
+        ps[0].W = LW(ONE_W_HX_GATE); ps[0].Nw = c.r; ps[0].K = HH; ps[0].X = B_(e->b.o); ps[0].ldx = HH;
+        ps[0].bias = nullptr; ps[0].out = B_(e->b.ghx); ps[0].ldo = c.r;
+        ps[1].W = LW(ONE_W_X_GATE); ps[1].Nw = c.r; ps[1].K = HH; ps[1].X = B_(e->b.o); ps[1].ldx = HH;
+        ps[1].bias = nullptr; ps[1].out = B_(e->b.gx); ps[1].ldo = c.r;
+        Launch g;
+        int rc = plan_gemm(g, ps, 2, T, dt, err);
+        if (rc) return rc;
+        plan.push_back(g);
+        const int k = c.top_k;
+        int* ridx = e->at<int>(e->b.ridx);
+        MoeRouter R[3];
+        memset(R, 0, sizeof(R));
+        R[0].glog = B_(e->b.ghx); R[0].experts = LW(ONE_W_HX_EXPERTS); R[0].bias2 = LW(ONE_W_HX_BIAS2);
+        R[0].x = B_(e->b.o); R[0].ldx = HH; R[0].in = HH; R[0].comb = B_(e->b.comb_hx); R[0].idx_out = ridx;
+        R[1].glog = B_(e->b.gx); R[1].experts = LW(ONE_W_X_EXPERTS); R[1].bias2 = LW(ONE_W_X_BIAS2);
+        R[1].x = B_(e->b.o); R[1].ldx = HH; R[1].in = HH; R[1].comb = B_(e->b.comb_x);
+        R[1].idx_out = ridx + (size_t)T * k;
+        R[2].glog = B_(e->b.gcx); R[2].experts = LW(ONE_W_CX_EXPERTS); R[2].bias2 = LW(ONE_W_CX_BIAS2);
+        R[2].x = B_(e->b.cxc[cur]); R[2].ldx = D; R[2].in = D; R[2].comb = B_(e->b.comb_cx);
+        R[2].idx_out = ridx + (size_t)2 * T * k;
+        for (int i = 0; i < 3; ++i) {
+          Launch rl;
+          rc = plan_router(rl, R[i], T, c.r, c.num_experts, k, dt);
+          if (rc) return rc;
+          plan.push_back(rl);
+        }
+      }
+    } else {
       Launch a;
       a.kind = L_ROW_ATTN;
       a.dtype = dt;
@@ -943,6 +1077,18 @@ extern "C" int one_engine_step(one_engine* e, int32_t batch, const int32_t* ids,
   e->step_graphs.push_back(sg);
   CK(cudaGraphLaunch(sg.x, (cudaStream_t)stream));
   return ONE_OK;
+}
+
+extern "C" int32_t one_engine_prefill_launches(one_engine* e, int32_t batch, int32_t seq_len, int32_t logits_mode) {
+  if (!e || batch < 1 || seq_len < 1) return -1;
+  std::vector<Launch> plan;
+  if (build_layers(e, plan, batch * seq_len, false, seq_len, batch, nullptr, false, nullptr)) return -1;
+  link_splits(plan);
+  int32_t dummy = 0;
+  if (build_final(e, plan, batch * seq_len, batch, seq_len, logits_mode != 2, logits_mode ? &dummy : nullptr, false,
+                  nullptr))
+    return -1;
+  return (int32_t)plan.size() + 1;  // + the counter update
 }
 
 extern "C" int32_t one_engine_step_launches(one_engine* e, int32_t batch) {

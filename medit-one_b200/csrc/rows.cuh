@@ -898,7 +898,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
               w = isnan(w) ? 1.0f / (float)H : rnd<T>(w);
               const float ov = rnd<T>(w * vv[q]);
               o[h * H + j] = ov;
-              xs[h * H + j] = fminf(fmaxf(ov, -1e4f), 1e4f);  // LinearMoE clamp (:53)
+              xs[h * H + j] = moe_clamp<T>(ov);  // LinearMoE clamp (:53)
             }
           }
         }
@@ -968,7 +968,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
         w = isnan(w) ? 1.0f / (float)H : rnd<T>(w);
         const float ov = rnd<T>(w * v);
         reinterpret_cast<float*>(tb + L.tk.o)[h * H + lane] = ov;
-        reinterpret_cast<float*>(tb + L.tk.xs)[h * H + lane] = fminf(fmaxf(ov, -1e4f), 1e4f);  // LinearMoE clamp (:53)
+        reinterpret_cast<float*>(tb + L.tk.xs)[h * H + lane] = moe_clamp<T>(ov);  // LinearMoE clamp (:53)
       }
     }
     __syncthreads();
@@ -1176,7 +1176,7 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const MoeRouter R, int 
   const int kk = min(k, E);
   auto load_x = [&](int t) {
     const T* X = reinterpret_cast<const T*>(R.x) + (size_t)t * R.ldx;
-    for (int i = lane; i < in; i += 32) xs[i] = fminf(fmaxf(ld<T>(X + i), -1e4f), 1e4f);  // (:53)
+    for (int i = lane; i < in; i += 32) xs[i] = moe_clamp<T>(ld<T>(X + i));  // (:53)
   };
   group = max(1, min(32, group));
   for (int t0 = (blockIdx.x * nwarp + warp) * group; t0 < ntok; t0 += gridDim.x * nwarp * group) {

@@ -48,6 +48,7 @@ SIGNATURES = {
     "one_engine_buffer": (c_void_p, [c_void_p, c_char_p]),
     "one_engine_error": (c_int, [c_void_p, POINTER(c_int32), POINTER(c_int32)]),
     "one_engine_step_launches": (c_int32, [c_void_p, c_int32]),
+    "one_engine_prefill_launches": (c_int32, [c_void_p, c_int32, c_int32, c_int32]),
     "one_engine_profile_step": (c_int32, [c_void_p, c_int32, c_int32, POINTER(c_float), c_int32, c_void_p]),
     "one_linear_moe_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "one_linear_moe": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -234,6 +234,13 @@ class OneEngine:
     def step_launches(self, batch: Optional[int] = None) -> int:
         return int(C.LIB.one_engine_step_launches(self.h, batch or self.batch))
 
+    def prefill_launches(self, batch: int, seq_len: int, logits: str = "none") -> int:
+        """Kernels one prefill(ids [batch, seq_len], logits) launches: per layer row_pre, prefix-mean
+        scan, GEMM A, attention (+ gate GEMM and three router launches on the prompt path), GEMM C,
+        gate/up, down; the RoPE table; the final row_pre, up_scaler, norm, lm_head; the counter update."""
+        mode = {"none": 0, "last": 1, "all": 2}[logits]
+        return int(C.LIB.one_engine_prefill_launches(self.h, batch, seq_len, mode))
+
     # ------------------------------------------------------------------ API
     def reset(self, batch: int, pos: int = 0) -> None:
         C.check(C.LIB.one_engine_reset(self.h, batch, pos, self._stream()), "one_engine_reset")

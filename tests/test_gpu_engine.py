@@ -116,6 +116,28 @@ def test_140m_decode_matches_oracle_bf16():
     assert eng.device_error() == (0, 0)
 
 
+def test_140m_prefill_matches_oracle_bf16():
+    """140M-class model, 2 prompts x 96 tokens through prompt ingestion (warp-per-token
+    attention, tensor-core hx/x gate logits, one router launch per LinearMoE): the logits of
+    every position and the last layer's hx / cx against the oracle's forward."""
+    from one.configuration_one import config_140m
+    from one.initialization import init_state_dict
+    from oracle import one_oracle as O
+    from test_oracle_golden import ocfg
+    cfg = config_140m()
+    sd = init_state_dict(cfg, 6, torch.bfloat16)
+    ids = torch.randint(0, 32000, (2, 96), generator=torch.Generator().manual_seed(6))
+    ref = O.forward(sd, ids, ocfg(cfg), torch.bfloat16)
+    eng = make_engine(cfg, sd, "bf16", max_batch=2, max_tokens=192)
+    lg = eng.prefill(ids.cuda(), logits="all")
+    torch.cuda.synchronize()
+    assert eng.device_error() == (0, 0)
+    assert_close(lg.float().cpu().numpy(), ref.logits.float().numpy(), "bf16", "logits")
+    hx, cx = eng.last_hx_cx(192)
+    assert_close(hx.float().cpu().view(2, 96, -1).numpy(), ref.hx.float().numpy(), "bf16", "hx")
+    assert_close(cx.float().cpu().view(2, 96, -1).numpy(), ref.cx.float().numpy(), "bf16", "cx")
+
+
 def test_graph_replay_equals_stepwise():
     """A captured multi-step greedy graph reproduces step-by-step greedy decode."""
     from one.configuration_one import tiny_config

@@ -63,6 +63,35 @@ def test_linear_moe_large_matches_oracle(dt):
     assert_close(y.float().cpu().numpy(), y_ref.float().numpy(), dt, "LinearMoE output")
 
 
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+def test_router_clamps_large_inputs_like_reference(dt):
+    """Inputs beyond +-1e4 (one/linear_moe.py:53): x.clamp(-1e4, 1e4) of a bf16 tensor gives
+    bf16(1e4) = 9984. Through the LinearMoE op, and through the router entry on the unclamped
+    input with the reference's gate logits (the router applies the clamp itself)."""
+    import ctypes
+    import torch.nn.functional as F
+    from one import _capi as C
+    from one.initialization import moe_params
+    from oracle import one_oracle as O
+    p = moe_params(144, 64, 8, 64, 7, DT[dt])
+    x = (torch.randn(256, 144, generator=torch.Generator().manual_seed(7)) * 8000.0).to(DT[dt])
+    assert (x.float().abs() > 1e4).float().mean() > 0.1
+    y_ref, idx_ref = O.linear_moe(x, p, 2)
+    y, idx = native_linear_moe(x.cuda(), p, 2)
+    np.testing.assert_array_equal(idx.cpu().long().numpy(), idx_ref.numpy())
+    assert_close(y.float().cpu().numpy(), y_ref.float().numpy(), dt, "LinearMoE output")
+    gl = F.linear(x.clamp(-1e4, 1e4), p["gate"]).cuda()
+    pc = {kk: v.cuda().contiguous() for kk, v in p.items()}
+    xd = x.cuda()
+    comb = torch.empty(256, 144, dtype=DT[dt], device="cuda")
+    idx2 = torch.empty(256, 2, dtype=torch.int32, device="cuda")
+    C.check(C.LIB.one_moe_routing(C.ptr(xd), 256, 144, C.ptr(gl), C.ptr(pc["experts"]), C.ptr(pc["bias2"]), 8, 64, 2,
+                                  C.dtype_code(DT[dt]), C.ptr(comb), C.ptr(idx2),
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "one_moe_routing")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(idx2.cpu().long().numpy(), idx_ref.numpy())
+
+
 def test_linear_moe_all_ties_reference_order():
     """Random-init LinearMoE (bias2 = 0, small experts): every score ties; the reference
     keeps the experts std::nth_element leaves in front."""
