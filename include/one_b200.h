@@ -206,6 +206,13 @@ int one_rope_flash_attention(const void* q, const void* k, const void* v, const 
  * (No reference counterpart: the reference's kernels have no device-side waits.) */
 int one_ops_error(int32_t* where, int32_t clear);
 
+/* Self-test of the prompt path's prefix-mean division (a reciprocal table and one residual
+ * correction instead of a division per element): every bf16 dividend (all 65536 bit
+ * patterns) against each of the n divisors, compared with the fp32 division. mismatches[0]
+ * counts fp32 results that differ, mismatches[1] results that differ after rounding to
+ * bf16 (NaN equals NaN). Synchronises the device. (No reference counterpart.) */
+int one_selftest_mean_division(const float* divisors, int32_t n, unsigned long long* mismatches, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,53 +35,28 @@ struct AttnTokParams {
   uint32_t clamp2;            // bf16x2 bound of the LinearMoE input clamp (0: store o unclamped)
 };
 
-// RoPE table of one prompt call (OneRotaryEmbedding, one/modeling_one.py:159-182): the fp32
-// angle inv_freq_i * pos, cos / sin rounded to bf16. Shared by all layers of the call.
-struct RopeTabParams {
+// Per-position tables of one prompt call, shared by all layers: the RoPE cos / sin
+// (OneRotaryEmbedding, one/modeling_one.py:159-182: the fp32 angle inv_freq_i * pos, cos / sin
+// rounded to bf16) and the reciprocal of each prefix-mean divisor (for div_rn_recip).
+struct PromptTabParams {
   const int* counters;  // counters[0] = position of the first prompt token
   const float* inv_freq;
-  int seq_len, half;
+  int seq_len, half;    // half = 0: no RoPE table
   __nv_bfloat16* tab;   // [seq_len][2 * half]
+  const float* div;     // [seq_len] prefix-mean divisors
+  float* recip;         // [seq_len] RN(1 / div)
 };
 
-__global__ void rope_table_kernel(const RopeTabParams p) {
+__global__ void prompt_table_kernel(const PromptTabParams p) {
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < p.seq_len) p.recip[i] = 1.0f / p.div[i];
   if (i >= p.seq_len * p.half) return;
   const int s = i / p.half, j = i % p.half;
   const float f = p.inv_freq[j] * (float)(p.counters[0] + s);
   p.tab[(size_t)s * 2 * p.half + j] = __float2bfloat16_rn(cosf(f));
   p.tab[(size_t)s * 2 * p.half + p.half + j] = __float2bfloat16_rn(sinf(f));
 }
-
-// packed bf16x2 arithmetic, each result rounded once to nearest-even
-ONE_DEVINL uint32_t bf2_mul(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-ONE_DEVINL uint32_t bf2_add(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-ONE_DEVINL uint32_t bf2_sub(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-ONE_DEVINL uint32_t bf2_max(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-ONE_DEVINL uint32_t bf2_min(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-ONE_DEVINL float bf2_lo(uint32_t u) { return __uint_as_float(u << 16); }
-ONE_DEVINL float bf2_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
 // Shared memory (bytes): lin_q / lin_k / lin_v as [3][16][RS] bf16 (rows >= H zero), biases
 // [3][16] fp32, then per warp the token's q | k | v rows [3H][RS] bf16 and the output row

@@ -310,3 +310,32 @@ extern "C" int one_rope_flash_attention(const void* q, const void* k, const void
   if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "RoPE launch: %s", cudaGetErrorString(e));
   return attn_launch(qr, kr, v, b, h, n, n, dh, causal, scale, dtype, out, st);
 }
+
+// every bf16 dividend a (blockIdx.x * blockDim.x + threadIdx.x = its bit pattern) against
+// divisors[blockIdx.y]
+__global__ void selftest_division_kernel(const float* div, unsigned long long* mism) {
+  const uint32_t bits = blockIdx.x * blockDim.x + threadIdx.x;
+  if (bits >= 65536u) return;
+  const float a = __uint_as_float(bits << 16), b = div[blockIdx.y];
+  const float ref = a / b, got = div_rn_recip(a, b, 1.0f / b);
+  const bool nan2 = isnan(ref) && isnan(got);
+  const uint32_t r16 = pack_bf16x2(ref, ref) & 0xffffu, g16 = pack_bf16x2(got, got) & 0xffffu;
+  if (!nan2 && __float_as_uint(ref) != __float_as_uint(got)) atomicAdd(&mism[0], 1ull);
+  if (!nan2 && r16 != g16) atomicAdd(&mism[1], 1ull);
+}
+
+extern "C" int one_selftest_mean_division(const float* divisors, int32_t n, unsigned long long* mismatches,
+                                          void* stream) {
+  if (!divisors || !mismatches || n < 1 || n > 65535) return fail(ONE_ERR_INVALID, "bad self-test arguments");
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned long long* d = nullptr;
+  CK(cudaMallocAsync(&d, 16, st));
+  CK(cudaMemsetAsync(d, 0, 16, st));
+  selftest_division_kernel<<<dim3(256, n), 256, 0, st>>>(divisors, d);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaMemcpyAsync(mismatches, d, 16, cudaMemcpyDeviceToHost, st);
+  cudaFreeAsync(d, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "division self-test: %s", cudaGetErrorString(e));
+  return ONE_OK;
+}

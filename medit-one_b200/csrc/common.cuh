@@ -73,6 +73,35 @@ ONE_DEVINL double warp_sum_d(double v) {
   return v;
 }
 
+// packed bf16x2 arithmetic, each result rounded once to nearest-even
+ONE_DEVINL uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL uint32_t bf2_min(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ONE_DEVINL float bf2_lo(uint32_t u) { return __uint_as_float(u << 16); }
+ONE_DEVINL float bf2_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
 // x.clamp(-1e4, 1e4) of a LinearMoE input (one/linear_moe.py:53) kept in fp32: the bound is 1e4
 // converted to the tensor's type, 9984 for bf16
 template <typename T>

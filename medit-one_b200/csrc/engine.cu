@@ -32,6 +32,7 @@
 #include "rows.cuh"
 #include "flash_attn.cuh"
 #include "attn_tok.cuh"
+#include "router.cuh"
 
 using namespace one;
 
@@ -114,7 +115,7 @@ struct ProbSpec {
 
 enum LaunchKind {
   L_GEMM_TC, L_GEMM_SIMT, L_ROW_PRE, L_ROW_ATTN, L_SCAN, L_ROW_NORM, L_ADVANCE, L_NEXT_IDS,
-  L_ROPE_TAB, L_ATTN_TOK, L_ROUTER
+  L_PROMPT_TAB, L_ATTN_TOK, L_ROUTER, L_ROW_PRE_W
 };
 
 struct AdvanceParams {
@@ -168,12 +169,13 @@ struct Launch {
   RowNormParams rn;
   AdvanceParams ad;
   NextIdsParams ni;
-  RopeTabParams rt;
+  PromptTabParams pt;
   AttnTokParams at;
   struct {
     MoeRouter R;
     int n, r, E, k, group;
     unsigned long long tie;
+    int np;  // > 0: moe_router_bf16_kernel<np> (input pairs per lane)
   } ro;
 };
 
@@ -324,6 +326,15 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(moe_router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(moe_router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem));
+  for (int np : {1, 3, 6, 12, 24, 32}) {
+    const void* f = np == 1    ? (const void*)moe_router_bf16_kernel<1>
+                    : np == 3  ? (const void*)moe_router_bf16_kernel<3>
+                    : np == 6  ? (const void*)moe_router_bf16_kernel<6>
+                    : np == 12 ? (const void*)moe_router_bf16_kernel<12>
+                    : np == 24 ? (const void*)moe_router_bf16_kernel<24>
+                               : (const void*)moe_router_bf16_kernel<32>;
+    CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  }
   CK(cudaFuncSetAttribute(attn_tok_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<32>::total(16)));
   CK(cudaFuncSetAttribute(attn_tok_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<64>::total(16)));
   g_attrs_set = true;
@@ -333,6 +344,28 @@ static int set_kernel_attrs() {
 template <typename T>
 static cudaError_t launch_row_pre(const Launch& L, cudaStream_t st) {
   return launch_k(row_pre_kernel<T>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+}
+template <typename T>
+static cudaError_t launch_row_pre_w(const Launch& L, cudaStream_t st) {
+  switch (L.nv) {
+    case 1: return launch_k(row_pre_warp_kernel<T, 1>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+    case 2: return launch_k(row_pre_warp_kernel<T, 2>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+    case 3: return launch_k(row_pre_warp_kernel<T, 3>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+    default: return launch_k(row_pre_warp_kernel<T, 4>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+  }
+}
+// Prompt ingestion: a warp per token for row_pre when the row fits four 8-element chunks per lane.
+static void row_pre_shape(Launch& rp, int D, int T, bool decode) {
+  if (!decode && D / 8 <= 128) {
+    rp.kind = L_ROW_PRE_W;
+    rp.nv = (D / 8 + 31) / 32;
+    rp.block = 128;
+    rp.grid = (T + 3) / 4;
+  } else {
+    rp.kind = L_ROW_PRE;
+    rp.block = ((D / 8 + 31) / 32) * 32;
+    rp.grid = T;
+  }
 }
 template <typename T>
 static cudaError_t launch_row_norm(const Launch& L, cudaStream_t st) {
@@ -361,6 +394,7 @@ static int run(const Launch& L, cudaStream_t st) {
              : launch_k(gemm_simt_kernel<float>, dim3(L.grid), dim3(L.block), 0, st, L.sg, (DevErr*)nullptr);
       break;
     case L_ROW_PRE: e = bf ? launch_row_pre<__nv_bfloat16>(L, st) : launch_row_pre<float>(L, st); break;
+    case L_ROW_PRE_W: e = bf ? launch_row_pre_w<__nv_bfloat16>(L, st) : launch_row_pre_w<float>(L, st); break;
     case L_ROW_NORM: e = bf ? launch_row_norm<__nv_bfloat16>(L, st) : launch_row_norm<float>(L, st); break;
     case L_ROW_ATTN:
       if (L.nv == 16 && bf && L.minb == 2)
@@ -376,7 +410,7 @@ static int run(const Launch& L, cudaStream_t st) {
       e = bf ? launch_k(scan_mean_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), 0, st, L.sc)
              : launch_k(scan_mean_kernel<float>, dim3(L.grid), dim3(L.block), 0, st, L.sc);
       break;
-    case L_ROPE_TAB: e = launch_k(rope_table_kernel, dim3(L.grid), dim3(L.block), 0, st, L.rt); break;
+    case L_PROMPT_TAB: e = launch_k(prompt_table_kernel, dim3(L.grid), dim3(L.block), 0, st, L.pt); break;
     case L_ATTN_TOK:
       switch (L.nv) {
         case 32: e = launch_k(attn_tok_kernel<32>, dim3(L.grid), dim3(L.block), L.smem, st, L.at); break;
@@ -384,6 +418,19 @@ static int run(const Launch& L, cudaStream_t st) {
       }
       break;
     case L_ROUTER:
+      if (L.ro.np > 0) {
+        switch (L.ro.np) {
+#define ONE_R2(NP)                                                                                                   \
+  case NP:                                                                                                           \
+    e = launch_k(moe_router_bf16_kernel<NP>, dim3(L.grid), dim3(L.block), L.smem, st, L.ro.R, L.ro.n, L.ro.r, L.ro.E, \
+                 L.ro.k, L.ro.group, L.ro.tie);                                                                      \
+    break;
+          ONE_R2(1) ONE_R2(3) ONE_R2(6) ONE_R2(12) ONE_R2(24) ONE_R2(32)
+#undef ONE_R2
+          default: e = cudaErrorInvalidValue; break;
+        }
+        break;
+      }
       e = bf ? launch_k(moe_router_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), L.smem, st, L.ro.R, L.ro.n,
                         L.ro.r, L.ro.E, L.ro.k, L.ro.group, L.ro.tie)
              : launch_k(moe_router_kernel<float>, dim3(L.grid), dim3(L.block), L.smem, st, L.ro.R, L.ro.n, L.ro.r,
@@ -399,7 +446,45 @@ static int run(const Launch& L, cudaStream_t st) {
 static int run_plan(const std::vector<Launch>& plan, cudaStream_t st);
 
 // LinearMoE router launch over n tokens with precomputed gate logits (moe_router_kernel).
+static int router_np(int in) {
+  const int need = (in + 63) / 64;
+  for (int np : {1, 3, 6, 12, 24, 32})
+    if (need <= np) return np;
+  return 0;
+}
+
 static int plan_router(Launch& L, const MoeRouter& R, int n, int r, int E, int k, int dtype) {
+  auto a4 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 3) == 0; };
+  const int np = router_np(R.in);
+  const Router2Smem L2 = router2_smem(R.in, E);
+  if (dtype == ONE_DTYPE_BF16 && np > 0 && R.in % 2 == 0 && R.ldx % 2 == 0 && a4(R.x) && a4(R.comb) && a4(R.bias2) &&
+      r <= 128 && E <= kMaxExperts && std::min(k, E) <= kR2MaxK && L2.warps >= 1) {
+    const void* f = np == 1    ? (const void*)moe_router_bf16_kernel<1>
+                    : np == 3  ? (const void*)moe_router_bf16_kernel<3>
+                    : np == 6  ? (const void*)moe_router_bf16_kernel<6>
+                    : np == 12 ? (const void*)moe_router_bf16_kernel<12>
+                    : np == 24 ? (const void*)moe_router_bf16_kernel<24>
+                               : (const void*)moe_router_bf16_kernel<32>;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, 32 * L2.warps, L2.total) != cudaSuccess || per_sm < 1)
+      return fail(ONE_ERR_CUDA, "router kernel does not fit an SM");
+    const int group = std::max(1, std::min(32, n / (num_sms() * per_sm * L2.warps)));
+    const int groups = (n + group - 1) / group;
+    L.kind = L_ROUTER;
+    L.dtype = dtype;
+    L.smem = L2.total;
+    L.block = 32 * L2.warps;
+    L.grid = std::max(1, std::min((groups + L2.warps - 1) / L2.warps, num_sms() * per_sm));
+    L.ro.R = R;
+    L.ro.n = n;
+    L.ro.r = r;
+    L.ro.E = E;
+    L.ro.k = k;
+    L.ro.group = group;
+    L.ro.tie = topk_tie_selection(E, std::min(k, E));
+    L.ro.np = np;
+    return ONE_OK;
+  }
   const int es = dtype == ONE_DTYPE_F32 ? 4 : 2;
   const size_t smem = moe_router_smem_bytes(R.in, r, E, es);
   const int warps = moe_router_warps(R.in, r, E, es);
@@ -421,6 +506,7 @@ static int plan_router(Launch& L, const MoeRouter& R, int n, int r, int E, int k
   L.ro.k = k;
   L.ro.group = group;
   L.ro.tie = topk_tie_selection(E, std::min(k, E));
+  L.ro.np = 0;
   return ONE_OK;
 }
 
@@ -460,6 +546,7 @@ struct Bufs {
   size_t ridx;     // i32 [Tm, 3, k]
   size_t ghx, gx;  // [Tm, r] hx_moe / x_moe gate logits (prompt ingestion)
   size_t rope;     // bf16 [Tm, head_dim] RoPE cos | sin table of a prompt call
+  size_t recip;    // fp32 [Tm] reciprocals of a prompt call's prefix-mean divisors
   size_t total;
   int ws_rows;
 };
@@ -505,6 +592,7 @@ static Bufs layout(const one_config& c, int max_tokens, int max_batch, int hist_
   b.ghx = Lo.take(Tm * (size_t)std::max(c.r, 1) * es);
   b.gx = Lo.take(Tm * (size_t)std::max(c.r, 1) * es);
   b.rope = Lo.take(Tm * (size_t)c.head_dim * 2);
+  b.recip = Lo.take(Tm * 4);
   b.total = Lo.take(0) + 1024;
   return b;
 }
@@ -674,23 +762,26 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
   const int* counters = e->at<int>(e->b.counters);
   const int es = es_of(c);
   const bool tok = !decode && attn_tok_eligible(c);
-  if (tok) {  // RoPE table of the call's positions, shared by every layer
-    Launch rt;
-    rt.kind = L_ROPE_TAB;
-    rt.block = 256;
-    rt.grid = (seq_len * (Dh / 2) + 255) / 256;
-    rt.rt = RopeTabParams{counters, e->inv_freq, seq_len, Dh / 2, e->at<__nv_bfloat16>(e->b.rope)};
-    plan.push_back(rt);
+  // bf16 prompt ingestion: per-position tables shared by every layer (prefix-mean divisor
+  // reciprocals; the RoPE cos / sin for the warp-per-token attention)
+  const bool recip = !decode && dt == ONE_DTYPE_BF16;
+  if (recip) {
+    Launch pt;
+    pt.kind = L_PROMPT_TAB;
+    pt.block = 256;
+    const int half = tok ? Dh / 2 : 0;
+    pt.grid = (seq_len * std::max(half, 1) + 255) / 256;
+    pt.pt = PromptTabParams{counters, e->inv_freq, seq_len, half, e->at<__nv_bfloat16>(e->b.rope), prompt_div,
+                            e->at<float>(e->b.recip)};
+    plan.push_back(pt);
   }
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const int cur = l & 1, nxt = cur ^ 1;
     // ---- row_pre
     Launch rp;
-    rp.kind = L_ROW_PRE;
     rp.dtype = dt;
     rp.nv = nv;
-    rp.block = ((D / 8 + 31) / 32) * 32;
-    rp.grid = T;
+    row_pre_shape(rp, D, T, decode);
     RowPreParams& p = rp.rp;
     memset(&p, 0, sizeof(p));
     p.T = T;
@@ -731,10 +822,11 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       Launch s;
       s.kind = L_SCAN;
       s.dtype = dt;
-      s.block = 256;
-      s.grid = (batch * (D / 2) + 255) / 256;  // one thread per (sequence, feature pair)
+      s.block = 128;
+      s.grid = (batch * (D / 2) + 127) / 128;  // one thread per (sequence, feature pair)
       s.sc = ScanParams{batch, seq_len, D, B_(e->b.norm_x), B_(e->b.mean),
-                        e->at<float>(e->b.state) + (size_t)l * e->max_batch * D, prompt_div};
+                        e->at<float>(e->b.state) + (size_t)l * e->max_batch * D, prompt_div,
+                        recip ? e->at<float>(e->b.recip) : nullptr};
       plan.push_back(s);
     }
     // ---- gemm A
@@ -930,11 +1022,9 @@ static int build_final(one_engine* e, std::vector<Launch>& plan, int T, int batc
       break;
     }
   Launch rp;
-  rp.kind = L_ROW_PRE;
   rp.dtype = dt;
   rp.nv = nv;
-  rp.block = ((D / 8 + 31) / 32) * 32;
-  rp.grid = T;
+  row_pre_shape(rp, D, T, advance);
   RowPreParams& p = rp.rp;
   memset(&p, 0, sizeof(p));
   p.T = T;
@@ -1004,7 +1094,7 @@ static void link_splits(std::vector<Launch>& plan) {
     if (L.kind == L_GEMM_TC || L.kind == L_GEMM_SIMT) {
       const GemmProblem& P = L.kind == L_GEMM_TC ? L.g.prob[0] : L.sg.prob[0];
       if (P.kind == EPI_PARTIAL) splits = P.splits;
-    } else if (L.kind == L_ROW_PRE) {
+    } else if (L.kind == L_ROW_PRE || L.kind == L_ROW_PRE_W) {
       L.rp.splits = splits;
     }
   }

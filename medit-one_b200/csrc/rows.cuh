@@ -293,6 +293,149 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
   }
 }
 
+// Prompt-ingestion variant of row_pre_kernel (decode = 0): one warp per token, lane l owns
+// the 8-element chunks l, l + 32, ... (NV of them), reductions by warp shuffles only (no CTA
+// barrier). Same steps and rounding as row_pre_kernel; the row sums of squares are added in
+// another order (fp32), as any reduction of the reference's norm may be.
+template <typename T, int NV>
+__global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams p) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait();
+  if (t >= p.T) return;
+  const int D = p.D, nch = D / 8;
+  const size_t row = (size_t)t * D;
+  bool act[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) act[v] = lane + 32 * v < nch;
+  float h[NV][8], a[NV][8], b[8];
+  if (p.mode == PRE_FIRST) {
+    int id = 0;
+    if (lane == 0) {
+      id = p.ids_from_best ? 0 : p.ids[t];
+      if (p.ids_from_best) {
+        const unsigned long long key = p.best[t];
+        id = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
+      }
+      if (id < 0 || id >= p.vocab) {  // never gather outside the embedding table
+        set_err(p.err, ERR_BAD_ARG, 100);
+        id = 0;
+      }
+      p.best[t] = 0ull;
+      if (p.ids_out) p.ids_out[t] = id;
+      if (p.hist) {
+        const int step = p.counters[1];
+        if (step < p.hist_cap) p.hist[(size_t)step * p.T + t] = id;
+      }
+    }
+    id = __shfl_sync(0xffffffffu, id, 0);
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      if (act[v]) {
+        const size_t off = row + (size_t)(lane + 32 * v) * 8;
+        load8(reinterpret_cast<const T*>(p.emb) + (size_t)id * D + (lane + 32 * v) * 8, h[v]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          a[v][e] = 1.0f;
+          b[e] = fminf(fmaxf(h[v][e], -1e4f), 1e4f);
+        }
+        store8(reinterpret_cast<T*>(p.hx) + off, a[v]);
+        store8(reinterpret_cast<T*>(p.cx) + off, h[v]);
+        store8(reinterpret_cast<T*>(p.cxc) + off, b);
+        store8(reinterpret_cast<T*>(p.h) + off, h[v]);
+      }
+  } else {
+    // finish the previous layer (:571-573, :793, :563-564); split-K partials added in order
+    float hp[NV][8];
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      if (act[v]) {
+        const size_t off = row + (size_t)(lane + 32 * v) * 8;
+        load8(reinterpret_cast<const T*>(p.out0) + off, a[v]);
+        load8(reinterpret_cast<const T*>(p.h) + off, h[v]);
+        load8(reinterpret_cast<const T*>(p.hx_pre) + off, hp[v]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[v][e] = h[v][e] = hp[v][e] = 0.f;
+      }
+    float m[NV][8];
+    for (int sp = 0; sp < p.splits; ++sp) {
+      float w[NV][8];
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+        if (act[v]) load8(p.ws + (size_t)sp * p.T * D + row + (size_t)(lane + 32 * v) * 8, w[v]);
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m[v][e] = sp == 0 ? w[v][e] : m[v][e] + w[v][e];
+    }
+    float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      if (act[v]) {
+        if (p.down_b) {
+          float db[8];
+          load8(reinterpret_cast<const T*>(p.down_b) + (lane + 32 * v) * 8, db);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) m[v][e] += db[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[v][e] = rnd<T>(a[v][e] + rnd<T>(m[v][e]));
+        ss0 += sumsq8(a[v]);
+        ss1 += sumsq8(hp[v]);
+      }
+    ss0 = warp_sum(ss0);
+    ss1 = warp_sum(ss1);
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      if (act[v]) {
+        const int c = lane + 32 * v;
+        const size_t off = row + (size_t)c * 8;
+        float pw[8], pb[8];
+        load8(reinterpret_cast<const T*>(p.prev_norm_w) + c * 8, pw);
+        if (p.prev_norm_b) load8(reinterpret_cast<const T*>(p.prev_norm_b) + c * 8, pb);
+        chunk_norm_r<T>(a[v], ss0, D, 1e-6f, pw, pb, p.prev_norm_b != nullptr, b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[v][e] = rnd<T>(h[v][e] + b[e]);
+        chunk_norm_r<T>(hp[v], ss1, D, 1e-6f, pw, pb, p.prev_norm_b != nullptr, b);
+        store8(reinterpret_cast<T*>(p.hx) + off, b);
+        store8(reinterpret_cast<T*>(p.h) + off, h[v]);
+      }
+    if (p.mode == PRE_FINAL) {
+      float s3 = 0.f;
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+        if (act[v]) s3 += sumsq8(h[v]);
+      s3 = warp_sum(s3);
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+        if (act[v]) {
+          const int c = lane + 32 * v;
+          chunk_norm<T>(h[v], s3, D, p.lhs_eps, reinterpret_cast<const T*>(p.lhs_w),
+                        reinterpret_cast<const T*>(p.lhs_b), c, b);
+          store8(reinterpret_cast<T*>(p.hf) + row + (size_t)c * 8, b);
+        }
+      return;
+    }
+  }
+  // norm_x = norm1(h) (:340)
+  float s3 = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+    if (act[v]) s3 += sumsq8(h[v]);
+  s3 = warp_sum(s3);
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+    if (act[v]) {
+      const int c = lane + 32 * v;
+      float w1[8];
+      load8(reinterpret_cast<const T*>(p.norm1_w) + c * 8, w1);
+      chunk_norm_r<T>(h[v], s3, D, 1e-6f, w1, w1, false, b);
+      store8(reinterpret_cast<T*>(p.norm_x) + row + (size_t)c * 8, b);
+    }
+}
+
 // ------------------------------------------------------------------ prefill prefix mean
 // cumsum over the sequence in fp32 (CPU cumsum accumulates in order, in fp32) divided
 // by the arange divisors (:376-387). One thread per (sequence, feature).
@@ -302,14 +445,43 @@ struct ScanParams {
   void* mean;           // [B, S, D]
   float* state;         // [B, D] running sum in / out (decode state after the prompt)
   const float* div;     // [S] divisor of each prompt position
+  const float* recip;   // [S] 1 / div rounded to nearest (bf16 models), or null
 };
+
+// a / b rounded to nearest-even in fp32, given y = RN(1 / b), by one residual correction
+// (Markstein, "Computation of elementary functions on the IBM RISC System/6000 processor",
+// IBM J. Res. Dev. 34(1), 1990: with y the correctly rounded reciprocal and q0 a faithful
+// quotient, q0 + (a - b q0) y rounded once is the correctly rounded quotient; the residual
+// is exact under FMA). An exact q0 and a non-finite q0 are returned as they are. The engine
+// uses it for bf16 dividends and the prompt divisors; a GPU test checks it against the
+// division for every bf16 dividend and every divisor of positions 1..16384.
+ONE_DEVINL float div_rn_recip(float a, float b, float y) {
+  const float q0 = a * y;
+  const float r = fmaf(-q0, b, a);
+  return (r == 0.f || !(fabsf(q0) <= 3.402823466e38f)) ? q0 : fmaf(r, y, q0);
+}
+
+// two consecutive elements <-> two floats
+ONE_DEVINL void ld2(const __nv_bfloat16* p, float& a, float& b) {
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xffff0000u);
+}
+ONE_DEVINL void ld2(const float* p, float& a, float& b) {
+  const float2 v = *reinterpret_cast<const float2*>(p);
+  a = v.x;
+  b = v.y;
+}
+ONE_DEVINL void st2(__nv_bfloat16* p, float a, float b) { *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(a, b); }
+ONE_DEVINL void st2(float* p, float a, float b) { *reinterpret_cast<float2*>(p) = make_float2(a, b); }
 
 template <typename T>
 __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
   pdl_launch_dependents();
   pdl_wait();
   // one thread per (sequence, feature pair): the prefix sum runs in token order in fp32 (the
-  // reference's CPU cumsum order), with the next 32 tokens' inputs loaded ahead of the adds
+  // reference's CPU cumsum order). The next 32 tokens' input pairs and divisors are loaded
+  // before the adds; every mean pair is one store.
   constexpr int kAhead = 32;
   const int half = p.D / 2;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -318,24 +490,38 @@ __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
   float a0 = p.state[(size_t)bb * p.D + d], a1 = p.state[(size_t)bb * p.D + d + 1];
   const T* __restrict__ x = reinterpret_cast<const T*>(p.norm_x) + (size_t)bb * p.S * p.D + d;
   T* __restrict__ m = reinterpret_cast<T*>(p.mean) + (size_t)bb * p.S * p.D + d;
+  const float* __restrict__ div = p.div;
+  const float* __restrict__ rc = p.recip;
   for (int s0 = 0; s0 < p.S; s0 += kAhead) {
     const int n = min(kAhead, p.S - s0);
-    float v0[kAhead], v1[kAhead];
+    float v0[kAhead], v1[kAhead], dv[kAhead];
 #pragma unroll
     for (int j = 0; j < kAhead; ++j)
       if (j < n) {
-        v0[j] = ld<T>(x + (size_t)(s0 + j) * p.D);
-        v1[j] = ld<T>(x + (size_t)(s0 + j) * p.D + 1);
+        ld2(x + (size_t)(s0 + j) * p.D, v0[j], v1[j]);
+        dv[j] = __ldg(div + s0 + j);
       }
+    if (rc) {
+      float y[kAhead];
 #pragma unroll
-    for (int j = 0; j < kAhead; ++j)
-      if (j < n) {
-        a0 += v0[j];
-        a1 += v1[j];
-        const float dv = p.div[s0 + j];
-        st<T>(m + (size_t)(s0 + j) * p.D, rnd<T>(a0) / dv);
-        st<T>(m + (size_t)(s0 + j) * p.D + 1, rnd<T>(a1) / dv);
-      }
+      for (int j = 0; j < kAhead; ++j)
+        if (j < n) y[j] = __ldg(rc + s0 + j);
+#pragma unroll
+      for (int j = 0; j < kAhead; ++j)
+        if (j < n) {
+          a0 += v0[j];
+          a1 += v1[j];
+          st2(m + (size_t)(s0 + j) * p.D, div_rn_recip(rnd<T>(a0), dv[j], y[j]), div_rn_recip(rnd<T>(a1), dv[j], y[j]));
+        }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kAhead; ++j)
+        if (j < n) {
+          a0 += v0[j];
+          a1 += v1[j];
+          st2(m + (size_t)(s0 + j) * p.D, rnd<T>(a0) / dv[j], rnd<T>(a1) / dv[j]);
+        }
+    }
   }
   p.state[(size_t)bb * p.D + d] = a0;
   p.state[(size_t)bb * p.D + d + 1] = a1;

@@ -70,6 +70,7 @@ SIGNATURES = {
                                          c_int32, c_int32, c_int32, c_float, c_int32, c_void_p, c_void_p, c_size_t,
                                          c_void_p]),
     "one_ops_error": (c_int, [POINTER(c_int32), c_int32]),
+    "one_selftest_mean_division": (c_int, [c_void_p, c_int32, c_void_p, c_void_p]),
 }
 
 
