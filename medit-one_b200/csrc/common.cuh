@@ -73,6 +73,13 @@ ONE_DEVINL double warp_sum_d(double v) {
   return v;
 }
 
+// Two floats rounded to bf16 and packed, `lo` in the low half (the lower address).
+ONE_DEVINL uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
 // packed bf16x2 arithmetic, each result rounded once to nearest-even
 ONE_DEVINL uint32_t bf2_mul(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -101,6 +108,36 @@ ONE_DEVINL uint32_t bf2_min(uint32_t a, uint32_t b) {
 }
 ONE_DEVINL float bf2_lo(uint32_t u) { return __uint_as_float(u << 16); }
 ONE_DEVINL float bf2_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// Sum of a[0..8) over the warp. Afterwards every lane holds the total of value
+// r2_slot(lane) = 4 * bit4 + 2 * bit3 + bit2 of its lane index (four lanes per value).
+ONE_DEVINL double warp_transpose_sum8(double (&a)[8]) {
+  const int lane = threadIdx.x & 31;
+  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const double send = u16 ? a[q] : a[q + 4];
+    const double keep = u16 ? a[q + 4] : a[q];
+    a[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const double send = u8 ? a[q] : a[q + 2];
+    const double keep = u8 ? a[q + 2] : a[q];
+    a[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const double send = u4 ? a[0] : a[1];
+    const double keep = u4 ? a[1] : a[0];
+    a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
+  a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
+  return a[0];
+}
+ONE_DEVINL int r2_slot(int lane) { return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1); }
+
+ONE_DEVINL uint32_t bf2_splat(float v) { return pack_bf16x2(v, v); }
 
 // x.clamp(-1e4, 1e4) of a LinearMoE input (one/linear_moe.py:53) kept in fp32: the bound is 1e4
 // converted to the tensor's type, 9984 for bf16
@@ -337,12 +374,6 @@ ONE_DEVINL float2 add2(float2 a, float2 b) {
 ONE_DEVINL float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-// Two floats rounded to bf16 and packed, `lo` in the low half (the lower address).
-ONE_DEVINL uint32_t pack_bf16x2(float lo, float hi) {
-  uint32_t d;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
   return d;
 }
 

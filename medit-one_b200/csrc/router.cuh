@@ -46,36 +46,6 @@ __host__ __device__ inline Router2Smem router2_smem(int in, int E) {
   return L;
 }
 
-// Sum of a[0..8) over the warp. Afterwards every lane holds the total of value
-// r2_slot(lane) = 4 * bit4 + 2 * bit3 + bit2 of its lane index (four lanes per value).
-ONE_DEVINL double warp_transpose_sum8(double (&a)[8]) {
-  const int lane = threadIdx.x & 31;
-  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const double send = u16 ? a[q] : a[q + 4];
-    const double keep = u16 ? a[q + 4] : a[q];
-    a[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const double send = u8 ? a[q] : a[q + 2];
-    const double keep = u8 ? a[q + 2] : a[q];
-    a[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-  {
-    const double send = u4 ? a[0] : a[1];
-    const double keep = u4 ? a[1] : a[0];
-    a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
-  a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
-  return a[0];
-}
-ONE_DEVINL int r2_slot(int lane) { return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1); }
-
-ONE_DEVINL uint32_t bf2_splat(float v) { return pack_bf16x2(v, v); }
-
 // NP = input pairs per lane (in <= 64 * NP); r <= 128; k <= kR2MaxK; E <= kMaxExperts.
 template <int NP>
 __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf16_kernel(const MoeRouter R, int ntok, int r, int E, int k,

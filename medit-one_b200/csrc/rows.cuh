@@ -725,69 +725,93 @@ ONE_DEVINL void warp_gate_factors(float* g, int r, const float* ex, int E, float
   }
   sum = warp_sum(sum);
   const float inv = 1.0f / sum;
+  if constexpr (sizeof(T) == 2) {
+    // rounded gate values as bf16x2 pairs (m = 0, 1) and (2, 3); products rnd(g * x_e) are
+    // one packed multiply each; per-expert totals by the transposed butterfly
+    const uint32_t gp0 = pack_bf16x2(gv[0] * inv, gv[1] * inv), gp1 = pack_bf16x2(gv[2] * inv, gv[3] * inv);
+    const bool two = r > 64;
+    const int slot = r2_slot(lane);
+    for (int e0 = 0; e0 < E; e0 += 8) {
+      double a[8];
 #pragma unroll
-  for (int m = 0; m < kPer; ++m) gv[m] = rnd<T>(gv[m] * inv);
-  for (int e0 = 0; e0 < E; e0 += 8) {
-    double acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      acc[e] = 0.0;
-      if (e0 + e < E) {
-        const float xe = ex[e0 + e];
-#pragma unroll
-        for (int m = 0; m < kPer; ++m)
-          if (lane + 32 * m < r) acc[e] += (double)rnd<T>(gv[m] * xe);
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t xe2 = e0 + e < E ? bf2_splat(ex[e0 + e]) : 0u;
+        const uint32_t p0 = bf2_mul(gp0, xe2);
+        a[e] = (double)bf2_lo(p0);
+        a[e] += (double)bf2_hi(p0);
+        if (two) {
+          const uint32_t p1 = bf2_mul(gp1, xe2);
+          a[e] += (double)bf2_lo(p1);
+          a[e] += (double)bf2_hi(p1);
+        }
+      }
+      const double tot = warp_transpose_sum8(a);
+      if ((lane & 3) == 0 && e0 + slot < E) {
+        const float scv = fminf(fmaxf(rnd<T>((float)tot / (float)r), -10.f), 10.f);
+        c[e0 + slot] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
       }
     }
+    __syncwarp();
+  } else {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
-    double mine = acc[0];
+    for (int m = 0; m < kPer; ++m) gv[m] = rnd<T>(gv[m] * inv);
+    for (int e0 = 0; e0 < E; e0 += 8) {
+      double acc[8];
 #pragma unroll
-    for (int e = 1; e < 8; ++e)
-      if (lane == e) mine = acc[e];
-    if (lane < 8 && e0 + lane < E) {
-      const float scv = fminf(fmaxf(rnd<T>((float)mine / (float)r), -10.f), 10.f);
-      c[e0 + lane] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
+      for (int e = 0; e < 8; ++e) {
+        acc[e] = 0.0;
+        if (e0 + e < E) {
+          const float xe = ex[e0 + e];
+#pragma unroll
+          for (int m = 0; m < kPer; ++m)
+            if (lane + 32 * m < r) acc[e] += (double)rnd<T>(gv[m] * xe);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
+      double mine = acc[0];
+#pragma unroll
+      for (int e = 1; e < 8; ++e)
+        if (lane == e) mine = acc[e];
+      if (lane < 8 && e0 + lane < E) {
+        const float scv = fminf(fmaxf(rnd<T>((float)mine / (float)r), -10.f), 10.f);
+        c[e0 + lane] = rnd<T>(1.0f + rnd<T>(silu_f(scv)));
+      }
     }
+    __syncwarp();
   }
-  __syncwarp();
 }
 
-// Per-expert partial sums over x[i0..i1) of rnd(rnd(x * c_e) + bias2[e, i]) for experts
-// e0..e0+7, reduced over the warp (exact fp64). Result valid in every lane. bf16 with even
-// bounds and 4-byte aligned rows: each lane takes input pairs, reads bias2 as bf16x2 and
-// rounds both sums with one packed conversion. The terms are bf16 numbers, so their fp64
-// sum is exact in any order and the result does not depend on the pairing.
+// Per-expert sums over x[i0..i1) of rnd(rnd(x * c_e) + bias2[e, i]) for experts e0..e0+7,
+// reduced over the warp (exact fp64); returns the total of expert e0 + r2_slot(lane). bf16
+// with even bounds and 4-byte aligned rows: each lane takes input pairs, rounds x * c_e and
+// the biased sum as packed bf16x2 operations (the inputs are bf16 values) and adds both
+// halves in fp64. The terms are bf16 numbers, so their fp64 sum does not depend on the order.
 template <typename T>
-ONE_DEVINL void warp_expert_sums(const float* x, int i0, int i1, const T* B2, int in, const float* c, int e0, int E,
-                                 double (&acc)[8]) {
+ONE_DEVINL double warp_expert_sums_t(const float* x, int i0, int i1, const T* B2, int in, const float* c, int e0, int E) {
   const int lane = threadIdx.x & 31;
+  double acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.0;
   const int ne = min(8, E - e0);
   if (sizeof(T) == 2 && ((i0 | i1 | in) & 1) == 0 && (reinterpret_cast<uintptr_t>(B2) & 3) == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 7) == 0) {
-    float ce[8];
+    uint32_t c2[8];
     const uint32_t* brow[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      ce[e] = e < ne ? c[e0 + e] : 1.0f;
+      c2[e] = e < ne ? bf2_splat(c[e0 + e]) : 0u;
       brow[e] = reinterpret_cast<const uint32_t*>(B2 + (size_t)(e0 + (e < ne ? e : 0)) * in);
     }
     for (int i = i0 + 2 * lane; i < i1; i += 64) {
       const float2 xv = *reinterpret_cast<const float2*>(x + i);
+      const uint32_t xp = pack_bf16x2(xv.x, xv.y);
 #pragma unroll
       for (int e = 0; e < 8; ++e)
         if (e < ne) {
-          float2 xc = xv;
-          if (ce[e] != 1.0f) {
-            const uint32_t q = pack_bf16x2(xv.x * ce[e], xv.y * ce[e]);
-            xc = make_float2(__uint_as_float(q << 16), __uint_as_float(q & 0xffff0000u));
-          }
-          const uint32_t bw = brow[e][i >> 1];
-          const uint32_t r = pack_bf16x2(xc.x + __uint_as_float(bw << 16), xc.y + __uint_as_float(bw & 0xffff0000u));
-          acc[e] += (double)__uint_as_float(r << 16);
-          acc[e] += (double)__uint_as_float(r & 0xffff0000u);
+          const uint32_t r = bf2_add(bf2_mul(xp, c2[e]), brow[e][i >> 1]);
+          acc[e] += (double)bf2_lo(r);
+          acc[e] += (double)bf2_hi(r);
         }
     }
   } else {
@@ -802,8 +826,7 @@ ONE_DEVINL void warp_expert_sums(const float* x, int i0, int i1, const T* B2, in
         }
     }
   }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) acc[e] = warp_sum_d(acc[e]);
+  return warp_transpose_sum8(acc);
 }
 
 // mean of the selected biased inputs over x[i0..i1) (one/linear_moe.py:87-90): fp32 sum in
@@ -812,22 +835,32 @@ template <typename T>
 ONE_DEVINL void warp_combine(const float* x, int i0, int i1, const T* B2, int in, const float* c, const int* sel, int kk,
                              T* out) {
   const int lane = threadIdx.x & 31;
-  if (sizeof(T) == 2 && ((i0 | i1 | in) & 1) == 0 && (reinterpret_cast<uintptr_t>(B2) & 3) == 0 &&
+  if (sizeof(T) == 2 && kk <= 8 && ((i0 | i1 | in) & 1) == 0 && (reinterpret_cast<uintptr_t>(B2) & 3) == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
+    // packed: rnd(x * c_e) and the biased sum as bf16x2 operations, fp32 sums in selection order
+    uint32_t c2[8];
+    const uint32_t* brow[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = j < kk ? sel[j] : 0;
+      c2[j] = bf2_splat(c[e]);
+      brow[j] = reinterpret_cast<const uint32_t*>(B2 + (size_t)e * in);
+    }
+    const bool pow2 = (kk & (kk - 1)) == 0;
+    const float invk = 1.0f / (float)kk;
     for (int i = i0 + 2 * lane; i < i1; i += 64) {
       const float2 xv = *reinterpret_cast<const float2*>(x + i);
+      const uint32_t xp = pack_bf16x2(xv.x, xv.y);
       float s0 = 0.f, s1 = 0.f;
-      for (int j = 0; j < kk; ++j) {
-        const int e = sel[j];
-        const float ce = c[e];
-        const uint32_t q = pack_bf16x2(xv.x * ce, xv.y * ce);
-        const uint32_t bw = *reinterpret_cast<const uint32_t*>(B2 + (size_t)e * in + i);
-        const uint32_t r = pack_bf16x2(__uint_as_float(q << 16) + __uint_as_float(bw << 16),
-                                       __uint_as_float(q & 0xffff0000u) + __uint_as_float(bw & 0xffff0000u));
-        s0 += __uint_as_float(r << 16);
-        s1 += __uint_as_float(r & 0xffff0000u);
-      }
-      *reinterpret_cast<uint32_t*>(out + i) = pack_bf16x2(s0 / (float)kk, s1 / (float)kk);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < kk) {
+          const uint32_t r = bf2_add(bf2_mul(xp, c2[j]), brow[j][i >> 1]);
+          s0 += bf2_lo(r);
+          s1 += bf2_hi(r);
+        }
+      *reinterpret_cast<uint32_t*>(out + i) =
+          pow2 ? pack_bf16x2(s0 * invk, s1 * invk) : pack_bf16x2(s0 / (float)kk, s1 / (float)kk);
     }
     return;
   }
@@ -1231,12 +1264,9 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
           warp_gate_factors<T>(g, r, exps + ri * E, E, c, cp);
           const T* B2 = b2s + b2off[ri];
           for (int e0 = 0; e0 < E; e0 += 8) {
-            double acc[8];
-            warp_expert_sums<T>(xs, 0, HH, B2, HH, c, e0, E, acc);
-            if (lane == 0)
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                if (e0 + e < E) sc[ri * E + e0 + e] = rnd<T>(__double2float_rn(acc[e]));
+            const double tot = warp_expert_sums_t<T>(xs, 0, HH, B2, HH, c, e0, E);
+            const int sl = e0 + r2_slot(lane);
+            if ((lane & 3) == 0 && sl < E) sc[ri * E + sl] = rnd<T>(__double2float_rn(tot));
           }
           __syncwarp();
           if (lane == 0) {
@@ -1264,12 +1294,9 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
           const int i0 = q * qlen, i1 = min(D, i0 + qlen);
           const T* B2 = b2s + b2off[2];
           for (int e0 = 0; e0 < E; e0 += 8) {
-            double acc[8];
-            warp_expert_sums<T>(cxs, i0, i1, B2, D, c, e0, E, acc);
-            if (lane == 0)
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                if (e0 + e < E) part[q * kMaxExperts + e0 + e] = acc[e];
+            const double tot = warp_expert_sums_t<T>(cxs, i0, i1, B2, D, c, e0, E);
+            const int sl = e0 + r2_slot(lane);
+            if ((lane & 3) == 0 && sl < E) part[q * kMaxExperts + sl] = tot;
           }
           named_bar(bar, 32 * kAttnCxWarps);
           if (q == 0 && lane == 0) {
@@ -1376,12 +1403,9 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const MoeRouter R, int 
       float* c = cf + u * E;
       warp_gate_factors<T>(g, r, ex, E, c, cp);  // softmax (:56), expert factors (:59-68)
       for (int e0 = 0; e0 < E; e0 += 8) {        // exact per-expert sums (:71-80)
-        double acc[8];
-        warp_expert_sums<T>(xs, 0, in, B2, in, c, e0, E, acc);
-        if (lane == 0)
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (e0 + e < E) sc[u * E + e0 + e] = rnd<T>(__double2float_rn(acc[e]));
+        const double tot = warp_expert_sums_t<T>(xs, 0, in, B2, in, c, e0, E);
+        const int sl = e0 + r2_slot(lane);
+        if ((lane & 3) == 0 && sl < E) sc[u * E + sl] = rnd<T>(__double2float_rn(tot));
       }
       __syncwarp();
     }
