@@ -72,183 +72,207 @@ struct AttnTokSmem {
   __host__ __device__ static int total(int H) { return WARP0 + kTokWarps * per_warp(H); }
 };
 
-// Fragment layout of the projections: m16n8k16 with rows = heads g and g + 8, columns =
-// outputs. Within each 16-wide k slice, lane (g, c) supplies the logical k = 4c..4c+3 (one
-// 8-byte load) as the hardware's k = {2c, 2c+1, 2c+8, 2c+9}; A and B use the same
-// assignment, so every product pairs the same (k) elements.
+// Stage lin_q / lin_k / lin_v ([3][16][RS] bf16, rows >= H zero) and their biases ([3][16]
+// fp32) into shared memory, all threads of the CTA.
 template <int DH>
-__global__ void __launch_bounds__(kTokWarps * 32, 2) attn_tok_kernel(const AttnTokParams p) {
-  using S = AttnTokSmem<DH>;
-  constexpr int RS = S::RS, NS = DH / 16, HALF = DH / 2, NCH = DH / 8;
-  constexpr int kMaxLd = (3 * 16 * NCH + 31) / 32;
-  extern __shared__ __align__(16) uint8_t smb[];
-  const int H = p.H, HD = H * DH, HH = H * H;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, c = lane & 3;
-  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(smb + S::W);
-  float* bs = reinterpret_cast<float*>(smb + S::BIAS);
-
-  // weights (never written by the preceding kernels): staged before the dependency wait
-  for (int v = tid; v < 3 * 16 * NCH; v += blockDim.x) {
+ONE_DEVINL void stage_head_proj(__nv_bfloat16* ws, float* bs, int H, const __nv_bfloat16* wq, const __nv_bfloat16* bq,
+                                const __nv_bfloat16* wk, const __nv_bfloat16* bk, const __nv_bfloat16* wv,
+                                const __nv_bfloat16* bv) {
+  constexpr int RS = DH + 16, NCH = DH / 8;
+  for (int v = threadIdx.x; v < 3 * 16 * NCH; v += blockDim.x) {
     const int row = v / NCH, ch = v % NCH, pj = row / 16, n = row % 16;
     uint4 val = make_uint4(0u, 0u, 0u, 0u);
     if (n < H) {
-      const __nv_bfloat16* W = pj == 0 ? p.wq : pj == 1 ? p.wk : p.wv;
+      const __nv_bfloat16* W = pj == 0 ? wq : pj == 1 ? wk : wv;
       val = *reinterpret_cast<const uint4*>(W + (size_t)n * DH + ch * 8);
     }
     *reinterpret_cast<uint4*>(ws + row * RS + ch * 8) = val;
   }
-  for (int i = tid; i < 3 * 16; i += blockDim.x) {
+  for (int i = threadIdx.x; i < 3 * 16; i += blockDim.x) {
     const int pj = i / 16, n = i % 16;
-    const __nv_bfloat16* B = pj == 0 ? p.bq : pj == 1 ? p.bk : p.bv;
+    const __nv_bfloat16* B = pj == 0 ? bq : pj == 1 ? bk : bv;
     bs[i] = n < H ? __bfloat162float(B[n]) : 0.f;
   }
+}
+
+// One warp copies a token's q | k | v row ([3 * H * DH] bf16) into rows [3H][RS].
+template <int DH>
+ONE_DEVINL void load_token_rows(const __nv_bfloat16* src_row, int H, __nv_bfloat16* rows) {
+  constexpr int RS = DH + 16, NCH = DH / 8, kMaxLd = (3 * 16 * NCH + 31) / 32;
+  const int lane = threadIdx.x & 31, nch = 3 * H * NCH;
+  const uint4* src = reinterpret_cast<const uint4*>(src_row);
+  uint4 v[kMaxLd];
+#pragma unroll
+  for (int m = 0; m < kMaxLd; ++m) {
+    const int j = lane + 32 * m;
+    if (j < nch) v[m] = src[j];
+  }
+#pragma unroll
+  for (int m = 0; m < kMaxLd; ++m) {
+    const int j = lane + 32 * m;
+    if (j < nch) *reinterpret_cast<uint4*>(rows + (j / NCH) * RS + (j % NCH) * 8) = v[m];
+  }
+}
+
+// Fragment layout of the projections: m16n8k16 with rows = heads g and g + 8, columns =
+// outputs. Within each 16-wide k slice, lane (g, c) supplies the logical k = 4c..4c+3 (one
+// 8-byte load) as the hardware's k = {2c, 2c+1, 2c+8, 2c+9}; A and B use the same
+// assignment, so every product pairs the same (k) elements. cs / sn: the lane's cos / sin
+// pairs of indices 16 ls + 4c + {0, 1} (.x) and {2, 3} (.y), ls < DH / 32.
+//
+// One token by one warp: rows = the token's q | k | v ([3H][RS] bf16), ws / bs the staged
+// projections; writes the output row (clamped to +-clamp2 when clamp2 != 0) as bf16 pairs
+// into stage[H*H/2].
+template <int DH>
+ONE_DEVINL void attn_token_warp(const __nv_bfloat16* rows, const uint2 (&cs)[DH / 32], const uint2 (&sn)[DH / 32],
+                                const __nv_bfloat16* ws, const float* bs, int H, float scale, uint32_t scale2,
+                                int scale_exact, uint32_t clamp2, uint32_t* stage) {
+  constexpr int RS = DH + 16, NS = DH / 16;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const bool two_nt = H > 8;
+  const uint32_t negc = clamp2 ^ 0x80008000u;
+  float acc[3][2][4];
+#pragma unroll
+  for (int pj = 0; pj < 3; ++pj)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[pj][nt][q] = 0.f;
+#pragma unroll
+  for (int pj = 0; pj < 3; ++pj) {
+    uint32_t a[NS][4];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int h = g + 8 * rr;
+      const bool ok = h < H;
+      const __nv_bfloat16* rw = rows + (pj * H + (ok ? h : 0)) * RS + 4 * c;
+#pragma unroll
+      for (int ls = 0; ls < NS / 2; ++ls) {
+        uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
+        if (ok) {
+          lo = *reinterpret_cast<const uint2*>(rw + ls * 16);
+          hi = *reinterpret_cast<const uint2*>(rw + (ls + NS / 2) * 16);
+        }
+        if (pj < 2) {
+          if (pj == 0) {  // single_x * scale (:405)
+            if (scale_exact) {
+              lo = make_uint2(bf2_mul(lo.x, scale2), bf2_mul(lo.y, scale2));
+              hi = make_uint2(bf2_mul(hi.x, scale2), bf2_mul(hi.y, scale2));
+            } else {
+              lo = make_uint2(pack_bf16x2(bf2_lo(lo.x) * scale, bf2_hi(lo.x) * scale),
+                              pack_bf16x2(bf2_lo(lo.y) * scale, bf2_hi(lo.y) * scale));
+              hi = make_uint2(pack_bf16x2(bf2_lo(hi.x) * scale, bf2_hi(hi.x) * scale),
+                              pack_bf16x2(bf2_lo(hi.y) * scale, bf2_hi(hi.y) * scale));
+            }
+          }
+          // x * cos + rotate_half(x) * sin: out[d] = x[d] cos - x[d + half] sin,
+          // out[d + half] = x[d + half] cos + x[d] sin (cos / sin of index d)
+          const uint2 rl = make_uint2(bf2_sub(bf2_mul(lo.x, cs[ls].x), bf2_mul(hi.x, sn[ls].x)),
+                                      bf2_sub(bf2_mul(lo.y, cs[ls].y), bf2_mul(hi.y, sn[ls].y)));
+          const uint2 rh = make_uint2(bf2_add(bf2_mul(hi.x, cs[ls].x), bf2_mul(lo.x, sn[ls].x)),
+                                      bf2_add(bf2_mul(hi.y, cs[ls].y), bf2_mul(lo.y, sn[ls].y)));
+          lo = rl;
+          hi = rh;
+        }
+        a[ls][rr] = lo.x;
+        a[ls][rr + 2] = lo.y;
+        a[ls + NS / 2][rr] = hi.x;
+        a[ls + NS / 2][rr + 2] = hi.y;
+      }
+    }
+    const __nv_bfloat16* wrow = ws + pj * 16 * RS + 4 * c;
+#pragma unroll
+    for (int ks = 0; ks < NS; ++ks)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+        if (nt == 0 || two_nt) {
+          const uint2 b = *reinterpret_cast<const uint2*>(wrow + (nt * 8 + g) * RS + ks * 16);
+          mma_16816_bf16(acc[pj][nt], a[ks], b.x, b.y);
+        }
+  }
+
+  // lane (g, c): heads h = g + 8 rr, outputs j = 8 nt + 2c + {0, 1}
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int h = g + 8 * rr;
+    uint32_t lg[2], vv[2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int j = nt * 8 + 2 * c;
+      const uint32_t q2 = pack_bf16x2(acc[0][nt][2 * rr] + bs[j], acc[0][nt][2 * rr + 1] + bs[j + 1]);
+      const uint32_t k2 = pack_bf16x2(acc[1][nt][2 * rr] + bs[16 + j], acc[1][nt][2 * rr + 1] + bs[16 + j + 1]);
+      vv[nt] = pack_bf16x2(acc[2][nt][2 * rr] + bs[32 + j], acc[2][nt][2 * rr + 1] + bs[32 + j + 1]);
+      const uint32_t m = (j < H ? 0u : 0xffffu) | (j + 1 < H ? 0u : 0xffff0000u);
+      lg[nt] = (bf2_mul(q2, k2) & ~m) | (0xff80ff80u & m);  // masked outputs: -inf
+    }
+    uint32_t m2 = bf2_max(lg[0], lg[1]);
+    float mx = fmaxf(bf2_lo(m2), bf2_hi(m2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const uint32_t mx2 = pack_bf16x2(mx, mx);
+    uint32_t d1[2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) d1[nt] = bf2_sub(lg[nt], mx2);
+    m2 = bf2_max(d1[0], d1[1]);
+    float mm = fmaxf(bf2_lo(m2), bf2_hi(m2));
+    mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
+    mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
+    float ex[4], sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int nt = q >> 1, j = nt * 8 + 2 * c + (q & 1);
+      const float d = (q & 1) ? bf2_hi(d1[nt]) : bf2_lo(d1[nt]);
+      ex[q] = j < H ? expf(d - mm) : 0.f;
+      sum += ex[q];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float inv = 1.0f / sum;
+    if (h < H) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int j = nt * 8 + 2 * c;
+        if (j < H) {
+          float w0 = ex[2 * nt] * inv, w1 = ex[2 * nt + 1] * inv;
+          if (isnan(w0)) w0 = 1.0f / (float)H;
+          if (isnan(w1)) w1 = 1.0f / (float)H;
+          uint32_t o2 = bf2_mul(pack_bf16x2(w0, w1), vv[nt]);
+          if (clamp2) o2 = bf2_min(bf2_max(o2, negc), clamp2);  // LinearMoE clamp (one/linear_moe.py:53)
+          stage[(h * H + j) >> 1] = o2;
+        }
+      }
+    }
+  }
+}
+
+template <int DH>
+__global__ void __launch_bounds__(kTokWarps * 32, 2) attn_tok_kernel(const AttnTokParams p) {
+  using S = AttnTokSmem<DH>;
+  constexpr int RS = S::RS, HALF = DH / 2;
+  extern __shared__ __align__(16) uint8_t smb[];
+  const int H = p.H, HD = H * DH, HH = H * H;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c = lane & 3;
+  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(smb + S::W);
+  float* bs = reinterpret_cast<float*>(smb + S::BIAS);
+  // weights (never written by the preceding kernels): staged before the dependency wait
+  stage_head_proj<DH>(ws, bs, H, p.wq, p.bq, p.wk, p.bk, p.wv, p.bv);
   __syncthreads();
   pdl_wait();
 
   uint8_t* wb = smb + S::WARP0 + warp * S::per_warp(H);
   __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(wb);
   uint32_t* stage = reinterpret_cast<uint32_t*>(wb + 3 * H * RS * 2);
-  const int nch = 3 * H * NCH;  // 16-byte chunks of one token's q | k | v row
-  const bool two_nt = H > 8;
-  const uint32_t negc = p.clamp2 ^ 0x80008000u;
   for (int t = blockIdx.x * kTokWarps + warp; t < p.T; t += gridDim.x * kTokWarps) {
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(p.proj + (size_t)t * 3 * HD);
-      uint4 v[kMaxLd];
-#pragma unroll
-      for (int m = 0; m < kMaxLd; ++m) {
-        const int j = lane + 32 * m;
-        if (j < nch) v[m] = src[j];
-      }
-#pragma unroll
-      for (int m = 0; m < kMaxLd; ++m) {
-        const int j = lane + 32 * m;
-        if (j < nch) *reinterpret_cast<uint4*>(rows + (j / NCH) * RS + (j % NCH) * 8) = v[m];
-      }
-    }
+    load_token_rows<DH>(p.proj + (size_t)t * 3 * HD, H, rows);
     const __nv_bfloat16* tab = p.rope + (size_t)(t % p.seq_len) * DH;
-    uint2 cs[NS / 2], sn[NS / 2];
+    uint2 cs[DH / 32], sn[DH / 32];
 #pragma unroll
-    for (int ls = 0; ls < NS / 2; ++ls) {
+    for (int ls = 0; ls < DH / 32; ++ls) {
       cs[ls] = *reinterpret_cast<const uint2*>(tab + ls * 16 + 4 * c);
       sn[ls] = *reinterpret_cast<const uint2*>(tab + HALF + ls * 16 + 4 * c);
     }
     __syncwarp();
-
-    float acc[3][2][4];
-#pragma unroll
-    for (int pj = 0; pj < 3; ++pj)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[pj][nt][q] = 0.f;
-#pragma unroll
-    for (int pj = 0; pj < 3; ++pj) {
-      uint32_t a[NS][4];
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int h = g + 8 * rr;
-        const bool ok = h < H;
-        const __nv_bfloat16* rw = rows + (pj * H + (ok ? h : 0)) * RS + 4 * c;
-#pragma unroll
-        for (int ls = 0; ls < NS / 2; ++ls) {
-          uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
-          if (ok) {
-            lo = *reinterpret_cast<const uint2*>(rw + ls * 16);
-            hi = *reinterpret_cast<const uint2*>(rw + (ls + NS / 2) * 16);
-          }
-          if (pj < 2) {
-            if (pj == 0) {  // single_x * scale (:405)
-              if (p.scale_exact) {
-                lo = make_uint2(bf2_mul(lo.x, p.scale2), bf2_mul(lo.y, p.scale2));
-                hi = make_uint2(bf2_mul(hi.x, p.scale2), bf2_mul(hi.y, p.scale2));
-              } else {
-                const float sc = p.scale;
-                lo = make_uint2(pack_bf16x2(bf2_lo(lo.x) * sc, bf2_hi(lo.x) * sc),
-                                pack_bf16x2(bf2_lo(lo.y) * sc, bf2_hi(lo.y) * sc));
-                hi = make_uint2(pack_bf16x2(bf2_lo(hi.x) * sc, bf2_hi(hi.x) * sc),
-                                pack_bf16x2(bf2_lo(hi.y) * sc, bf2_hi(hi.y) * sc));
-              }
-            }
-            // x * cos + rotate_half(x) * sin: out[d] = x[d] cos - x[d + half] sin,
-            // out[d + half] = x[d + half] cos + x[d] sin (cos / sin of index d)
-            const uint2 rl = make_uint2(bf2_sub(bf2_mul(lo.x, cs[ls].x), bf2_mul(hi.x, sn[ls].x)),
-                                        bf2_sub(bf2_mul(lo.y, cs[ls].y), bf2_mul(hi.y, sn[ls].y)));
-            const uint2 rh = make_uint2(bf2_add(bf2_mul(hi.x, cs[ls].x), bf2_mul(lo.x, sn[ls].x)),
-                                        bf2_add(bf2_mul(hi.y, cs[ls].y), bf2_mul(lo.y, sn[ls].y)));
-            lo = rl;
-            hi = rh;
-          }
-          a[ls][rr] = lo.x;
-          a[ls][rr + 2] = lo.y;
-          a[ls + NS / 2][rr] = hi.x;
-          a[ls + NS / 2][rr + 2] = hi.y;
-        }
-      }
-      const __nv_bfloat16* wrow = ws + pj * 16 * RS + 4 * c;
-#pragma unroll
-      for (int ks = 0; ks < NS; ++ks)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-          if (nt == 0 || two_nt) {
-            const uint2 b = *reinterpret_cast<const uint2*>(wrow + (nt * 8 + g) * RS + ks * 16);
-            mma_16816_bf16(acc[pj][nt], a[ks], b.x, b.y);
-          }
-    }
-
-    // lane (g, c): heads h = g + 8 rr, outputs j = 8 nt + 2c + {0, 1}
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const int h = g + 8 * rr;
-      uint32_t lg[2], vv[2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int j = nt * 8 + 2 * c;
-        const uint32_t q2 = pack_bf16x2(acc[0][nt][2 * rr] + bs[j], acc[0][nt][2 * rr + 1] + bs[j + 1]);
-        const uint32_t k2 = pack_bf16x2(acc[1][nt][2 * rr] + bs[16 + j], acc[1][nt][2 * rr + 1] + bs[16 + j + 1]);
-        vv[nt] = pack_bf16x2(acc[2][nt][2 * rr] + bs[32 + j], acc[2][nt][2 * rr + 1] + bs[32 + j + 1]);
-        const uint32_t m = (j < H ? 0u : 0xffffu) | (j + 1 < H ? 0u : 0xffff0000u);
-        lg[nt] = (bf2_mul(q2, k2) & ~m) | (0xff80ff80u & m);  // masked outputs: -inf
-      }
-      uint32_t m2 = bf2_max(lg[0], lg[1]);
-      float mx = fmaxf(bf2_lo(m2), bf2_hi(m2));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const uint32_t mx2 = pack_bf16x2(mx, mx);
-      uint32_t d1[2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) d1[nt] = bf2_sub(lg[nt], mx2);
-      m2 = bf2_max(d1[0], d1[1]);
-      float mm = fmaxf(bf2_lo(m2), bf2_hi(m2));
-      mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
-      mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
-      float ex[4], sum = 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int nt = q >> 1, j = nt * 8 + 2 * c + (q & 1);
-        const float d = (q & 1) ? bf2_hi(d1[nt]) : bf2_lo(d1[nt]);
-        ex[q] = j < H ? expf(d - mm) : 0.f;
-        sum += ex[q];
-      }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      const float inv = 1.0f / sum;
-      if (h < H) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int j = nt * 8 + 2 * c;
-          if (j < H) {
-            float w0 = ex[2 * nt] * inv, w1 = ex[2 * nt + 1] * inv;
-            if (isnan(w0)) w0 = 1.0f / (float)H;
-            if (isnan(w1)) w1 = 1.0f / (float)H;
-            uint32_t o2 = bf2_mul(pack_bf16x2(w0, w1), vv[nt]);
-            if (p.clamp2) o2 = bf2_min(bf2_max(o2, negc), p.clamp2);  // LinearMoE clamp (one/linear_moe.py:53)
-            stage[(h * H + j) >> 1] = o2;
-          }
-        }
-      }
-    }
+    attn_token_warp<DH>(rows, cs, sn, ws, bs, H, p.scale, p.scale2, p.scale_exact, p.clamp2, stage);
     __syncwarp();
     uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (size_t)t * HH);
     for (int w = lane; w < HH / 2; w += 32) dst[w] = stage[w];

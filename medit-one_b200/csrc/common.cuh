@@ -414,7 +414,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int M, int N) { retur
 
 // ------------------------------------------------------------------ programmatic dependent launch
 // griddepcontrol is a no-op when the launch carries no programmatic dependency.
+// bar.sync counts whole warps and must be reached by converged warps: __syncwarp first, so
+// that lanes returning from divergent code (a lane-0 selection, a ragged loop) arrive together.
 ONE_DEVINL void named_barrier_sync(int id, int nthreads) {
+  __syncwarp();
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 ONE_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -33,6 +33,7 @@
 #include "flash_attn.cuh"
 #include "attn_tok.cuh"
 #include "router.cuh"
+#include "dec_attn.cuh"
 
 using namespace one;
 
@@ -115,7 +116,7 @@ struct ProbSpec {
 
 enum LaunchKind {
   L_GEMM_TC, L_GEMM_SIMT, L_ROW_PRE, L_ROW_ATTN, L_SCAN, L_ROW_NORM, L_ADVANCE, L_NEXT_IDS,
-  L_PROMPT_TAB, L_ATTN_TOK, L_ROUTER, L_ROW_PRE_W
+  L_PROMPT_TAB, L_ATTN_TOK, L_ROUTER, L_ROW_PRE_W, L_DEC_ATTN
 };
 
 struct AdvanceParams {
@@ -170,6 +171,7 @@ struct Launch {
   AdvanceParams ad;
   NextIdsParams ni;
   PromptTabParams pt;
+  DecAttnParams da;
   AttnTokParams at;
   struct {
     MoeRouter R;
@@ -335,6 +337,8 @@ static int set_kernel_attrs() {
                                : (const void*)moe_router_bf16_kernel<32>;
     CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   }
+  CK(cudaFuncSetAttribute(dec_attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaFuncSetAttribute(dec_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(attn_tok_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<32>::total(16)));
   CK(cudaFuncSetAttribute(attn_tok_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<64>::total(16)));
   g_attrs_set = true;
@@ -409,6 +413,10 @@ static int run(const Launch& L, cudaStream_t st) {
     case L_SCAN:
       e = bf ? launch_k(scan_mean_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), 0, st, L.sc)
              : launch_k(scan_mean_kernel<float>, dim3(L.grid), dim3(L.block), 0, st, L.sc);
+      break;
+    case L_DEC_ATTN:
+      e = L.nv == 32 ? launch_k(dec_attn_kernel<32>, dim3(L.grid), dim3(L.block), L.smem, st, L.da)
+                     : launch_k(dec_attn_kernel<64>, dim3(L.grid), dim3(L.block), L.smem, st, L.da);
       break;
     case L_PROMPT_TAB: e = launch_k(prompt_table_kernel, dim3(L.grid), dim3(L.block), 0, st, L.pt); break;
     case L_ATTN_TOK:
@@ -512,6 +520,14 @@ static int plan_router(Launch& L, const MoeRouter& R, int n, int r, int E, int k
 
 // Prompt ingestion takes the warp-per-token attention kernel (attn_tok_kernel) for bf16
 // models with an even number of heads <= 16 and head_dim 32 or 64.
+// Decode steps of routed bf16 models with the same head shapes take dec_attn_kernel.
+static bool dec_attn_eligible(const one_config& c) {
+  const int H = c.num_attention_heads, HH = H * H;
+  return c.dtype == ONE_DTYPE_BF16 && c.num_experts > 0 && H >= 2 && H <= 16 && H % 2 == 0 &&
+         (c.head_dim == 32 || c.head_dim == 64) && c.r % 16 == 0 && c.r <= 128 && HH % 16 == 0 &&
+         c.transformer_dim % 8 == 0;
+}
+
 static bool attn_tok_eligible(const one_config& c) {
   const int H = c.num_attention_heads, Dh = c.head_dim;
   return c.dtype == ONE_DTYPE_BF16 && H >= 2 && H <= 16 && H % 2 == 0 && (Dh == 32 || Dh == 64);
@@ -851,7 +867,46 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
     // ---- attention + routers, prompt ingestion: warp-per-token attention writes o (the
     // LinearMoE-clamped copy when routed), then the hx_moe / x_moe gate logits on the tensor
     // cores and one router launch per LinearMoE
-    if (tok) {
+    if (decode && dec_attn_eligible(c)) {
+      Launch a;
+      a.kind = L_DEC_ATTN;
+      a.dtype = dt;
+      a.nv = Dh;
+      a.block = kDecThreads;
+      a.smem = Dh == 32 ? dec_layout<32>(H, c.r, c.num_experts, D).total : dec_layout<64>(H, c.r, c.num_experts, D).total;
+      if (a.smem > 200 * 1024) return fail(ONE_ERR_UNSUPPORTED, "decode attention/router tile exceeds shared memory");
+      a.grid = std::max(1, std::min((T + 1) / 2, num_sms()));
+      DecAttnParams& q = a.da;
+      memset(&q, 0, sizeof(q));
+      q.T = T; q.H = H; q.r = c.r; q.E = c.num_experts; q.k = c.top_k;
+      q.counters = counters;
+      q.inv_freq = e->inv_freq;
+      q.proj = e->at<__nv_bfloat16>(e->b.proj);
+      q.scale = 1.0f / sqrtf((float)Dh);
+      const __nv_bfloat16 sb = __float2bfloat16_rn(q.scale);
+      q.scale_exact = __bfloat162float(sb) == q.scale ? 1 : 0;
+      uint16_t sbits;
+      memcpy(&sbits, &sb, 2);
+      q.scale2 = (uint32_t)sbits * 0x10001u;
+      q.wq = (const __nv_bfloat16*)LW(ONE_W_LINQ_W); q.bq = (const __nv_bfloat16*)LW(ONE_W_LINQ_B);
+      q.wk = (const __nv_bfloat16*)LW(ONE_W_LINK_W); q.bk = (const __nv_bfloat16*)LW(ONE_W_LINK_B);
+      q.wv = (const __nv_bfloat16*)LW(ONE_W_LINV_W); q.bv = (const __nv_bfloat16*)LW(ONE_W_LINV_B);
+      const int k = c.top_k;
+      int* ridx = e->at<int>(e->b.ridx);
+      MoeRouter& r0 = q.rt[0];
+      r0.gate_w = LW(ONE_W_HX_GATE); r0.experts = LW(ONE_W_HX_EXPERTS); r0.bias2 = LW(ONE_W_HX_BIAS2);
+      r0.in = HH; r0.comb = B_(e->b.comb_hx); r0.idx_out = ridx;
+      MoeRouter& r1 = q.rt[1];
+      r1.gate_w = LW(ONE_W_X_GATE); r1.experts = LW(ONE_W_X_EXPERTS); r1.bias2 = LW(ONE_W_X_BIAS2);
+      r1.in = HH; r1.comb = B_(e->b.comb_x); r1.idx_out = ridx + (size_t)T * k;
+      MoeRouter& r2 = q.rt[2];
+      r2.glog = B_(e->b.gcx); r2.experts = LW(ONE_W_CX_EXPERTS); r2.bias2 = LW(ONE_W_CX_BIAS2);
+      r2.x = B_(e->b.cxc[cur]); r2.ldx = D; r2.in = D; r2.comb = B_(e->b.comb_cx);
+      r2.idx_out = ridx + (size_t)2 * T * k;
+      q.tie = topk_tie_selection(c.num_experts, std::min(c.top_k, c.num_experts));
+      q.err = err;
+      plan.push_back(a);
+    } else if (tok) {
       Launch a;
       a.kind = L_ATTN_TOK;
       a.dtype = dt;

@@ -658,7 +658,7 @@ ONE_DEVINL uint32_t pack_bf16(float lo, float hi) {
 }
 ONE_DEVINL uint32_t ldg_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
-ONE_DEVINL void named_bar(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
+ONE_DEVINL void named_bar(int id, int nthreads) { named_barrier_sync(id, nthreads); }
 
 // softmax over the r gate logits in g[] (fp32, cast to the dtype), then the expert
 // factors c_e = 1 + silu(clamp(mean_r(rnd(g * e)))) (one/linear_moe.py:56-68) into c[].
@@ -1299,17 +1299,20 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) row_attn_kernel(const RowA
             if ((lane & 3) == 0 && sl < E) part[q * kMaxExperts + sl] = tot;
           }
           named_bar(bar, 32 * kAttnCxWarps);
-          if (q == 0 && lane == 0) {
-            for (int e = 0; e < E; ++e) {
+          if (q == 0) {
+            for (int e = lane; e < E; e += 32) {  // the quarters' partials added in quarter order
               double s2 = 0.0;
               for (int qq = 0; qq < kAttnCxWarps; ++qq) s2 += part[qq * kMaxExperts + e];
               sc[2 * E + e] = rnd<T>(__double2float_rn(s2));
             }
-            int chosen[kMaxExperts];
-            topk_select_fast(sc + 2 * E, E, kk, chosen, p.tie);
-            for (int j = 0; j < kk; ++j) {
-              sel[2 * E + j] = chosen[j];
-              if (p.rt[2].idx_out) p.rt[2].idx_out[(size_t)t * kk + j] = chosen[j];
+            __syncwarp();
+            if (lane == 0) {
+              int chosen[kMaxExperts];
+              topk_select_fast(sc + 2 * E, E, kk, chosen, p.tie);
+              for (int j = 0; j < kk; ++j) {
+                sel[2 * E + j] = chosen[j];
+                if (p.rt[2].idx_out) p.rt[2].idx_out[(size_t)t * kk + j] = chosen[j];
+              }
             }
           }
           named_bar(bar, 32 * kAttnCxWarps);

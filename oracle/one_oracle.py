@@ -418,9 +418,17 @@ def layer_params(sd: Dict[str, Tensor], i: int, cfg: OracleConfig) -> Dict[str, 
     return lp
 
 
+# When a list, every routed LinearMoE call appends its top-k indices [tokens, k] (per layer:
+# hx_moe, x_moe, cx_moe), for tests that compare the engine's expert selections.
+ROUTE_LOG: Optional[List[Tensor]] = None
+
+
 def _moe(x: Tensor, p: Dict[str, Tensor], cfg: OracleConfig) -> Tensor:
     if cfg.use_moe:
-        return linear_moe(x, p, cfg.top_k_experts)[0]
+        y, idx = linear_moe(x, p, cfg.top_k_experts)
+        if ROUTE_LOG is not None:
+            ROUTE_LOG.append(idx.reshape(-1, idx.shape[-1]))
+        return y
     return F.linear(x, p["weight"], p["bias"])
 
 

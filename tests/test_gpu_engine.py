@@ -138,6 +138,61 @@ def test_140m_prefill_matches_oracle_bf16():
     assert_close(cx.float().cpu().view(2, 96, -1).numpy(), ref.cx.float().numpy(), "bf16", "cx")
 
 
+def routing_heavy(sd, seed):
+    """The LinearMoE tensors of a random-init state dict redrawn so that routing depends on the
+    token: experts ~ N(0, 30) (distinct factors 1 + silu(score)), bias2 = 0 (a bias would fix
+    the choice), gate ~ N(0, 0.2). Random-init experts make every score tie."""
+    g = torch.Generator().manual_seed(seed)
+    out = dict(sd)
+    for k, v in sd.items():
+        std = 30.0 if k.endswith(".experts") else 0.0 if k.endswith(".bias2") else \
+            0.2 if k.endswith(".gate.weight") else None
+        if std is not None:
+            out[k] = torch.empty(v.shape).normal_(0.0, std, generator=g).to(v.dtype)
+    return out
+
+
+def test_router_selections_match_oracle_bf16():
+    """Expert selections (the hx_moe, x_moe and cx_moe top-k, in the reference's order) of the
+    last layer of a two-layer 140M-class model with routing-heavy LinearMoE parameters: prompt
+    ingestion of 2 x 64 tokens, then 4 decode steps fed the oracle's greedy tokens. The router
+    inputs equal the oracle's up to fp32 summation order, so at least 99 % of the tokens' ordered
+    selections must be identical (a selection read before it is written fails this)."""
+    from one.configuration_one import config_140m
+    from one.initialization import init_state_dict
+    from oracle import one_oracle as O
+    from test_oracle_golden import ocfg
+    cfg = config_140m(num_hidden_layers=2)
+    sd = routing_heavy(init_state_dict(cfg, 8, torch.bfloat16), 9)
+    ids = torch.randint(0, 32000, (2, 64), generator=torch.Generator().manual_seed(8))
+    dec = O.RunningDecoder(sd, ocfg(cfg), torch.bfloat16)
+    eng = make_engine(cfg, sd, "bf16", max_batch=2, max_tokens=128)
+
+    def compare(log, T, what):
+        got = eng.router_idx(T).cpu().long()
+        for ri, name in enumerate(("hx_moe", "x_moe", "cx_moe")):
+            ref = log[-3 + ri].long()
+            same = (got[ri] == ref).all(-1).float().mean().item()
+            assert same >= 0.99, f"{what} {name}: {same:.3f} of the tokens select like the oracle"
+
+    O.ROUTE_LOG = []
+    try:
+        res = dec.prefill(ids)
+        eng.prefill(ids.cuda())
+        torch.cuda.synchronize()
+        compare(O.ROUTE_LOG, 128, "prefill")
+        for s in range(4):
+            nxt = res.logits[:, -1].argmax(-1)
+            O.ROUTE_LOG = []
+            res = dec.step(nxt.view(2, 1))
+            eng.step(nxt.cuda())
+            torch.cuda.synchronize()
+            compare(O.ROUTE_LOG, 2, f"step {s}")
+    finally:
+        O.ROUTE_LOG = None
+    assert eng.device_error() == (0, 0)
+
+
 def test_graph_replay_equals_stepwise():
     """A captured multi-step greedy graph reproduces step-by-step greedy decode."""
     from one.configuration_one import tiny_config
