@@ -6,9 +6,11 @@
 //   row_pre   finish layer l-1 (down_proj partial sums, residual, norm, hx norm),
 //             norm_x = norm1(h), running sum S_l += norm_x, mean = S_l / P
 //   gemm A    lin1(norm_x) | lin2(hx) | lin3(cx) | cx_moe.gate(clamp(cx))
-//   row_attn  RoPE feature attention, hx_moe / x_moe / cx_moe routers + combine
-//   gemm C    hx_moe -> hx + clamp(.)  |  x_moe -> mean * clamp(.)  |  cx_moe -> cx'
-//   gemm D    gate_proj / up_proj (row-interleaved) -> gelu(g) * u
+//   dec_attn  RoPE feature attention, hx_moe / x_moe / cx_moe routers + combine
+//             (prompt ingestion: attn_tok, the hx/x gate GEMM, three router launches)
+//   gemm C    x_moe -> mean * clamp(.)
+//   gemm D    gate_proj / up_proj (row-interleaved) -> gelu(g) * u  |  hx_moe -> hx + clamp(.)
+//             |  cx_moe -> cx'
 //   gemm E    down_proj, split-K fp32 partials
 // then row_pre(final) -> lhs_norm, gemm up_scaler, row_norm (model norm), gemm lm_head
 // with a fused argmax. Every launch carries the programmatic-stream-serialization
@@ -1013,31 +1015,33 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       q.err = err;
       plan.push_back(a);
     }
-    // ---- gemm C
+    // ---- gemm C: x_moe -> mean * clamp(.), the gate/up input. hx_moe and cx_moe are only
+    // read by the next layer, so they run inside the gate/up launch (gemm D) instead of
+    // lengthening this one (cx_moe has K = D, x_moe K = H*H).
+    {
+      ProbSpec ps[1];
+      ps[0].kind = EPI_XMOE; ps[0].W = LW(ONE_W_X_W); ps[0].Nw = D; ps[0].K = HH;
+      ps[0].X = moe ? B_(e->b.comb_x) : B_(e->b.o); ps[0].ldx = HH; ps[0].bias = LW(ONE_W_X_B);
+      ps[0].out = B_(e->b.out0); ps[0].ldo = D; ps[0].aux = B_(e->b.mean); ps[0].lda = D;
+      Launch g;
+      int rc = plan_gemm(g, ps, 1, T, dt, err);
+      if (rc) return rc;
+      plan.push_back(g);
+    }
+    // ---- gemm D: gate/up | hx_moe -> hx + clamp(.) | cx_moe -> cx' and its clamp
     {
       ProbSpec ps[3];
-      ps[0].kind = EPI_HXPRE; ps[0].W = LW(ONE_W_HX_W); ps[0].Nw = D; ps[0].K = HH;
-      ps[0].X = moe ? B_(e->b.comb_hx) : B_(e->b.o); ps[0].ldx = HH; ps[0].bias = LW(ONE_W_HX_B);
-      ps[0].out = B_(e->b.hx_pre); ps[0].ldo = D; ps[0].aux = B_(e->b.hx); ps[0].lda = D;
-      ps[1].kind = EPI_XMOE; ps[1].W = LW(ONE_W_X_W); ps[1].Nw = D; ps[1].K = HH;
-      ps[1].X = moe ? B_(e->b.comb_x) : B_(e->b.o); ps[1].ldx = HH; ps[1].bias = LW(ONE_W_X_B);
-      ps[1].out = B_(e->b.out0); ps[1].ldo = D; ps[1].aux = B_(e->b.mean); ps[1].lda = D;
+      ps[0].kind = EPI_GELU_UP; ps[0].W = LW(ONE_W_GATE_UP); ps[0].Nw = 2 * I; ps[0].K = D;
+      ps[0].X = B_(e->b.out0); ps[0].ldx = D; ps[0].bias = c.mlp_bias ? LW(ONE_W_GATE_UP_B) : nullptr;
+      ps[0].out = B_(e->b.act); ps[0].ldo = I;
+      ps[1].kind = EPI_HXPRE; ps[1].W = LW(ONE_W_HX_W); ps[1].Nw = D; ps[1].K = HH;
+      ps[1].X = moe ? B_(e->b.comb_hx) : B_(e->b.o); ps[1].ldx = HH; ps[1].bias = LW(ONE_W_HX_B);
+      ps[1].out = B_(e->b.hx_pre); ps[1].ldo = D; ps[1].aux = B_(e->b.hx); ps[1].lda = D;
       ps[2].kind = EPI_CX; ps[2].W = LW(ONE_W_CX_W); ps[2].Nw = D; ps[2].K = D;
       ps[2].X = moe ? B_(e->b.comb_cx) : B_(e->b.cx[cur]); ps[2].ldx = D; ps[2].bias = LW(ONE_W_CX_B);
       ps[2].out = B_(e->b.cx[nxt]); ps[2].ldo = D; ps[2].out2 = B_(e->b.cxc[nxt]); ps[2].ldo2 = D;
       Launch g;
       int rc = plan_gemm(g, ps, 3, T, dt, err);
-      if (rc) return rc;
-      plan.push_back(g);
-    }
-    // ---- gemm D: gate/up
-    {
-      ProbSpec ps[1];
-      ps[0].kind = EPI_GELU_UP; ps[0].W = LW(ONE_W_GATE_UP); ps[0].Nw = 2 * I; ps[0].K = D;
-      ps[0].X = B_(e->b.out0); ps[0].ldx = D; ps[0].bias = c.mlp_bias ? LW(ONE_W_GATE_UP_B) : nullptr;
-      ps[0].out = B_(e->b.act); ps[0].ldo = I;
-      Launch g;
-      int rc = plan_gemm(g, ps, 1, T, dt, err);
       if (rc) return rc;
       plan.push_back(g);
     }
