@@ -158,7 +158,8 @@ __global__ void next_ids_kernel(const NextIdsParams p) {
 
 struct Launch {
   LaunchKind kind;
-  int bn = 0;  // tensor-core tile width
+  int bn = 0;       // tensor-core tile width
+  int persist = 0;  // gemm_bf16_tc_persistent (one CTA per SM looping over the tiles)
   int minb = 1;  // row_attn: CTAs per SM the instantiation is compiled for
   int grid = 1, block = 1;
   size_t smem = 0;
@@ -239,6 +240,9 @@ static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, Dev
     P.T = T;
     P.m_tiles = (s.Nw + BM - 1) / BM;
     P.n_tiles = (T + BN - 1) / BN;
+    // many token tiles (prompt ingestion): weight tile fastest, so the CTAs running together
+    // share activation slabs in L2 (gemm_tile_coords)
+    P.m_fast = tc && P.n_tiles >= 2 * num_sms() ? 1 : 0;
     const int kb = (s.K + 63) / 64;
     int splits = 1;
     if (s.kind == EPI_PARTIAL && s.max_splits > 1) {
@@ -271,11 +275,19 @@ static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, Dev
       L.sg.ldx[i] = s.ldx;
     }
   }
+  bool argmax = false;
+  for (int i = 0; i < n; ++i) argmax |= ps[i].kind == EPI_ARGMAX;
   if (tc) {
     L.g.nprob = n;
     L.g.total_tiles = tiles;
     L.g.err = err;
     L.block = TcCfg<64>::kThreads;
+    if (BN == kPBN && !argmax && tiles >= 2 * num_sms()) {
+      L.persist = 1;
+      L.smem = PCfg::kSmem;
+      L.grid = num_sms();
+      return ONE_OK;
+    }
     switch (BN) {
       case 32: L.smem = TcCfg<32>::kSmem; break;
       case 64: L.smem = TcCfg<64>::kSmem; break;
@@ -320,6 +332,7 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<64>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<128>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::kSmem));
+  CK(cudaFuncSetAttribute(gemm_bf16_tc_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::kSmem));
   const int attn_max = 220 * 1024;
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -388,6 +401,10 @@ static int run(const Launch& L, cudaStream_t st) {
   const bool bf = L.dtype == ONE_DTYPE_BF16;
   switch (L.kind) {
     case L_GEMM_TC:
+      if (L.persist) {
+        e = launch_k(gemm_bf16_tc_persistent, dim3(L.grid), dim3(L.block), L.smem, st, L.g);
+        break;
+      }
       switch (L.bn) {
         case 32: e = launch_k(gemm_bf16_tc_kernel<32>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
         case 64: e = launch_k(gemm_bf16_tc_kernel<64>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;

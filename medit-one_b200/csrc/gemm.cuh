@@ -33,6 +33,7 @@ struct GemmProblem {
   int K;
   int T;             // tokens
   int m_tiles, n_tiles, splits, kb_per_split;
+  int m_fast;        // tile order: 1 = weight tile fastest (many token tiles), 0 = token tile fastest
   int tile_begin;    // first linear CTA index of this problem
   const void* bias;  // [Nw] model dtype, or null
   void* out;
@@ -446,6 +447,34 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
   }
 }
 
+// Linear tile index -> (problem, split, m tile, n tile, first k block, k blocks). Token tile
+// fastest (m_fast = 0: the CTAs that share a weight slice run together and the slice comes
+// from HBM once) for few token tiles; weight tile fastest (m_fast = 1) when the token tiles
+// are many, so the CTAs running at once share a few activation slabs in L2 instead of each
+// streaming its own slab from HBM once per weight tile.
+ONE_DEVINL void gemm_tile_coords(const GemmParams& p, int tile, int& pi, int& m_tile, int& n_tile, int& split, int& kb0,
+                                 int& nkb) {
+  pi = 0;
+  while (pi + 1 < p.nprob && tile >= p.prob[pi + 1].tile_begin) ++pi;
+  const GemmProblem& P = p.prob[pi];
+  int local = tile - P.tile_begin;
+  if (P.m_fast) {
+    m_tile = local % P.m_tiles;
+    local /= P.m_tiles;
+    n_tile = local % P.n_tiles;
+    local /= P.n_tiles;
+  } else {
+    n_tile = local % P.n_tiles;
+    local /= P.n_tiles;
+    m_tile = local % P.m_tiles;
+    local /= P.m_tiles;
+  }
+  split = local;
+  const int kb_total = (P.K + 63) / 64;
+  kb0 = split * P.kb_per_split;
+  nkb = min(kb0 + P.kb_per_split, kb_total) - kb0;
+}
+
 template <int BN>
 __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
   using C = TcCfg<BN>;
@@ -456,20 +485,10 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
   uint64_t* accb = empty + C::kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
 
-  // linear tile -> (problem, split, m tile, n tile); n fastest so the CTAs that share a
-  // weight slice run together and the slice is fetched from HBM once.
-  const int tile = blockIdx.x;
-  int pi = 0;
-  while (pi + 1 < p.nprob && tile >= p.prob[pi + 1].tile_begin) ++pi;
+  // linear tile -> (problem, split, m tile, n tile): gemm_tile_coords
+  int pi, m_tile, n_tile, split, kb0, nkb;
+  gemm_tile_coords(p, blockIdx.x, pi, m_tile, n_tile, split, kb0, nkb);
   const GemmProblem& P = p.prob[pi];
-  int local = tile - P.tile_begin;
-  const int n_tile = local % P.n_tiles;
-  local /= P.n_tiles;
-  const int m_tile = local % P.m_tiles;
-  const int split = local / P.m_tiles;
-  const int kb_total = (P.K + 63) / 64;
-  const int kb0 = split * P.kb_per_split;
-  const int nkb = min(kb0 + P.kb_per_split, kb_total) - kb0;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -545,6 +564,268 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, BN);
+  }
+}
+
+// ------------------------------------------------------------------ persistent tensor-core kernel
+// Large GEMMs (prompt ingestion, batched LinearMoE): one CTA per SM loops over the tiles
+// (tile = blockIdx.x + i * gridDim.x, the linear order above). Warp 0 streams A / B stages
+// through a kPStages-deep ring, warp 1 issues the MMAs into one of two TMEM accumulators
+// (columns [0, kPBN) and [kPBN, 2 kPBN)), and warps 2..5 drain the other accumulator through
+// their own staging tile and apply the epilogue, so a tile's epilogue runs under the next
+// tile's main loop. Same epilogue steps and rounding as tc_epilogue (no fused argmax).
+constexpr int kPStages = 4;
+constexpr int kPBN = 256;
+constexpr int kPChunk = 32;  // tokens per staging pass
+struct PCfg {
+  static constexpr int kABytes = 128 * 64 * 2;
+  static constexpr int kBBytes = kPBN * 64 * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStagingOff = kPStages * kStageBytes;
+  static constexpr int kStagingBytes = kPChunk * 128 * 4;
+  static constexpr int kBarOff = kStagingOff + kStagingBytes;
+  static constexpr int kSmem = kBarOff + 256 + 1024 /*align*/;
+  static constexpr int kThreads = 192;
+};
+static_assert(PCfg::kSmem <= 227 * 1024, "persistent GEMM shared memory");
+
+// One tile's epilogue by warps 2..5 (e = 0..127): TMEM quarter q = warp % 4, accumulator
+// columns [col0, col0 + kPBN), staged kPChunk tokens at a time through S.
+ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uint32_t col0, int m_tile, int n_tile,
+                              int split) {
+  using T = __nv_bfloat16;
+  constexpr int CH = kPChunk, NT = 128;
+  constexpr int TU = NT / 16, TG = NT / 8;  // tokens per pass: (token, 8-row) / gelu units
+  constexpr int KU = CH / TU, KG = CH / TG;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = warp & 3;
+  const int e = threadIdx.x - 64;
+  const int n_base = m_tile * 128, t_tile = n_tile * kPBN;
+  const int kind = P.kind;
+  const bool aux_kind = kind == EPI_HXPRE || kind == EPI_XMOE;
+  const int c8 = e & 15, n0 = n_base + c8 * 8;
+  const bool v8 = n0 < P.Nw;
+  float b8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (kind != EPI_GELU_UP && kind != EPI_PARTIAL && P.bias && v8) load8(reinterpret_cast<const T*>(P.bias) + n0, b8);
+  const int cg = e & 7, ng = n_base + cg * 16;
+  float bg[16] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+  if (kind == EPI_GELU_UP && P.bias && ng < P.Nw) {
+    load8(reinterpret_cast<const T*>(P.bias) + ng, bg);
+    load8(reinterpret_cast<const T*>(P.bias) + ng + 8, bg + 8);
+  }
+  for (int cc = 0; cc < kPBN; cc += CH) {
+    const int tn = min(CH, P.T - (t_tile + cc));
+    if (tn <= 0) break;
+    uint4 auxr[KU];
+#pragma unroll
+    for (int k = 0; k < KU; ++k) {
+      const int t = t_tile + cc + (e >> 4) + TU * k;
+      auxr[k] = make_uint4(0, 0, 0, 0);
+      if (aux_kind && v8 && t < P.T)
+        auxr[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0);
+    }
+    // ---- E1: this warp's TMEM lane quarter -> S[token][row]
+#pragma unroll
+    for (int c0 = 0; c0 < CH; c0 += 16) {
+      if (c0 >= tn) break;  // warp-uniform
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + col0 + (uint32_t)(cc + c0), v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
+    }
+    named_barrier_sync(1, NT);
+    // ---- E2
+    const int tb = t_tile + cc;
+    if (kind == EPI_GELU_UP) {
+      T* out = reinterpret_cast<T*>(P.out);
+#pragma unroll
+      for (int k = 0; k < KG; ++k) {
+        const int tl = (e >> 3) + TG * k;
+        if (tl >= tn || ng >= P.Nw) continue;
+        const float* sv = S + tl * 128 + cg * 16;
+        float o8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float gb = rnd<T>(sv[2 * j] + bg[2 * j]);
+          const float ub = rnd<T>(sv[2 * j + 1] + bg[2 * j + 1]);
+          o8[j] = rnd<T>(gelu_erf(gb)) * ub;
+        }
+        store8(out + (size_t)(tb + tl) * P.ldo + (ng >> 1), o8);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < KU; ++k) {
+        const int tl = (e >> 4) + TU * k;
+        if (tl >= tn || !v8) continue;
+        const int t = tb + tl;
+        float a[8];
+        {
+          const float4 f0 = *reinterpret_cast<const float4*>(S + tl * 128 + c8 * 8);
+          const float4 f1 = *reinterpret_cast<const float4*>(S + tl * 128 + c8 * 8 + 4);
+          a[0] = f0.x; a[1] = f0.y; a[2] = f0.z; a[3] = f0.w; a[4] = f1.x; a[5] = f1.y; a[6] = f1.z; a[7] = f1.w;
+        }
+        if (kind == EPI_PARTIAL) {
+          store8(P.ws + ((size_t)split * P.T + t) * P.ldw + n0, a);
+          continue;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] += b8[j];
+        T* out = reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n0;
+        if (kind == EPI_STORE) {
+          store8(out, a);
+        } else if (kind == EPI_CX) {
+          float y[8], z[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            y[j] = rnd<T>(a[j]);
+            z[j] = fminf(fmaxf(y[j], -1e4f), 1e4f);
+          }
+          store8(out, y);
+          store8(reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0, z);
+        } else {  // HXPRE: aux + clamp(y); XMOE: aux * clamp(y)
+          float x[8], y[8];
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&auxr[k]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h2[j]);
+            x[2 * j] = f.x;
+            x[2 * j + 1] = f.y;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float cl = fminf(fmaxf(rnd<T>(a[j]), -100.f), 100.f);
+            y[j] = kind == EPI_HXPRE ? x[j] + cl : x[j] * cl;
+          }
+          store8(out, y);
+        }
+      }
+    }
+    named_barrier_sync(1, NT);
+  }
+}
+
+__global__ void __launch_bounds__(192, 1) gemm_bf16_tc_persistent(const __grid_constant__ GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PCfg::kBarOff);
+  uint64_t* empty = full + kPStages;
+  uint64_t* accf = empty + kPStages;  // [2] accumulator b holds a finished tile
+  uint64_t* acce = accf + 2;          // [2] accumulator b drained by the epilogue
+  uint64_t* drain = acce + 2;         // the MMA thread's last commit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* eflag = reinterpret_cast<int*>(tmem_slot + 1);  // [4] epilogue warps' wait results
+  float* S = reinterpret_cast<float*>(smem + PCfg::kStagingOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kPBN);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0)
+    for (int i = 0; i < p.nprob; ++i) {
+      tma_prefetch_desc(&p.tmw[i]);
+      tma_prefetch_desc(&p.tmx[i]);
+    }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  auto sA = [&](int s) { return smem + s * PCfg::kStageBytes; };
+  auto sB = [&](int s) { return smem + s * PCfg::kStageBytes + PCfg::kABytes; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      pdl_wait();
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
+        int pi, m_tile, n_tile, split, kb0, nkb;
+        gemm_tile_coords(p, tile, pi, m_tile, n_tile, split, kb0, nkb);
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % kPStages;
+          const uint32_t ph = (uint32_t)(it / kPStages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 21)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], PCfg::kStageBytes);
+          tma_load_2d(sA(s), &p.tmw[pi], &full[s], (kb0 + i) * 64, m_tile * 128);
+          tma_load_2d(sB(s), &p.tmx[pi], &full[s], (kb0 + i) * 64, n_tile * kPBN);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, kPBN);
+      int it = 0, ti = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x, ++ti) {
+        int pi, m_tile, n_tile, split, kb0, nkb;
+        gemm_tile_coords(p, tile, pi, m_tile, n_tile, split, kb0, nkb);
+        const int b = ti & 1;
+        if (!mbar_wait(&acce[b], ((uint32_t)(ti >> 1) & 1u) ^ 1u, p.err, 22)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * kPBN);
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % kPStages;
+          const uint32_t ph = (uint32_t)(it / kPStages) & 1u;
+          if (!mbar_wait(&full[s], ph, p.err, 23)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(sA(s));
+          const uint64_t bd = umma_desc_sw128(sB(s));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&accf[b]);
+      }
+      // every MMA issued by this thread has completed before the teardown frees TMEM
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, 24);
+    }
+  } else {
+    pdl_wait();
+    int ti = 0;
+    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++ti) {
+      int pi, m_tile, n_tile, split, kb0, nkb;
+      gemm_tile_coords(p, tile, pi, m_tile, n_tile, split, kb0, nkb);
+      const int b = ti & 1;
+      // one waiter per warp; the four warps agree before they leave together
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&accf[b], (uint32_t)(ti >> 1) & 1u, p.err, 25);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (lane == 0) eflag[warp - 2] = ok ? 1 : 0;
+      named_barrier_sync(2, 128);
+      const bool all_ok = eflag[0] && eflag[1] && eflag[2] && eflag[3];
+      named_barrier_sync(2, 128);
+      if (!all_ok) break;
+      tc_fence_after();
+      tc_epilogue_p(p.prob[pi], S, tmem, (uint32_t)(b * kPBN), m_tile, n_tile, split);
+      tc_fence_before();
+      mbar_arrive(&acce[b]);
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * kPBN);
   }
 }
 
