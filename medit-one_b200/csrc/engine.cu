@@ -285,6 +285,7 @@ static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, Dev
     if (BN == kPBN && !argmax && tiles >= 2 * num_sms()) {
       L.persist = 1;
       L.smem = PCfg::kSmem;
+      L.block = PCfg::kThreads;
       L.grid = num_sms();
       return ONE_OK;
     }

@@ -571,9 +571,10 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
 // Large GEMMs (prompt ingestion, batched LinearMoE): one CTA per SM loops over the tiles
 // (tile = blockIdx.x + i * gridDim.x, the linear order above). Warp 0 streams A / B stages
 // through a kPStages-deep ring, warp 1 issues the MMAs into one of two TMEM accumulators
-// (columns [0, kPBN) and [kPBN, 2 kPBN)), and warps 2..5 drain the other accumulator through
-// their own staging tile and apply the epilogue, so a tile's epilogue runs under the next
-// tile's main loop. Same epilogue steps and rounding as tc_epilogue (no fused argmax).
+// (columns [0, kPBN) and [kPBN, 2 kPBN)), and two groups of four epilogue warps (2..5, 6..9)
+// drain the other accumulator, alternate kPChunk-token chunks each through its own staging
+// tile, so a tile's epilogue runs under the next tile's main loop. Same epilogue steps and
+// rounding as tc_epilogue (no fused argmax).
 constexpr int kPStages = 4;
 constexpr int kPBN = 256;
 constexpr int kPChunk = 32;  // tokens per staging pass
@@ -582,23 +583,25 @@ struct PCfg {
   static constexpr int kBBytes = kPBN * 64 * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStagingOff = kPStages * kStageBytes;
-  static constexpr int kStagingBytes = kPChunk * 128 * 4;
-  static constexpr int kBarOff = kStagingOff + kStagingBytes;
+  static constexpr int kStagingBytes = kPChunk * 128 * 4;  // per epilogue group
+  static constexpr int kBarOff = kStagingOff + 2 * kStagingBytes;
   static constexpr int kSmem = kBarOff + 256 + 1024 /*align*/;
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;  // TMA warp, MMA warp, 2 x 4 epilogue warps
 };
 static_assert(PCfg::kSmem <= 227 * 1024, "persistent GEMM shared memory");
 
-// One tile's epilogue by warps 2..5 (e = 0..127): TMEM quarter q = warp % 4, accumulator
-// columns [col0, col0 + kPBN), staged kPChunk tokens at a time through S.
+// One tile's epilogue by one group of four warps (grp 0: warps 2..5, grp 1: warps 6..9;
+// e = 0..127 within the group): TMEM quarter q = warp % 4, accumulator columns
+// [col0, col0 + kPBN); the group takes the chunks cc = (2 j + grp) * kPChunk, staged through S.
 ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uint32_t col0, int m_tile, int n_tile,
-                              int split) {
+                              int split, int grp) {
   using T = __nv_bfloat16;
   constexpr int CH = kPChunk, NT = 128;
   constexpr int TU = NT / 16, TG = NT / 8;  // tokens per pass: (token, 8-row) / gelu units
   constexpr int KU = CH / TU, KG = CH / TG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = warp & 3;
-  const int e = threadIdx.x - 64;
+  const int e = threadIdx.x - 64 - 128 * grp;
+  const int bar = 1 + grp;
   const int n_base = m_tile * 128, t_tile = n_tile * kPBN;
   const int kind = P.kind;
   const bool aux_kind = kind == EPI_HXPRE || kind == EPI_XMOE;
@@ -612,7 +615,7 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
     load8(reinterpret_cast<const T*>(P.bias) + ng, bg);
     load8(reinterpret_cast<const T*>(P.bias) + ng + 8, bg + 8);
   }
-  for (int cc = 0; cc < kPBN; cc += CH) {
+  for (int cc = grp * CH; cc < kPBN; cc += 2 * CH) {
     const int tn = min(CH, P.T - (t_tile + cc));
     if (tn <= 0) break;
     uint4 auxr[KU];
@@ -633,7 +636,7 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
 #pragma unroll
       for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
     }
-    named_barrier_sync(1, NT);
+    named_barrier_sync(bar, NT);
     // ---- E2
     const int tb = t_tile + cc;
     if (kind == EPI_GELU_UP) {
@@ -700,11 +703,11 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
         }
       }
     }
-    named_barrier_sync(1, NT);
+    named_barrier_sync(bar, NT);
   }
 }
 
-__global__ void __launch_bounds__(192, 1) gemm_bf16_tc_persistent(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(320, 1) gemm_bf16_tc_persistent(const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + PCfg::kBarOff);
@@ -713,7 +716,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tc_persistent(const __grid_c
   uint64_t* acce = accf + 2;          // [2] accumulator b drained by the epilogue
   uint64_t* drain = acce + 2;         // the MMA thread's last commit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  int* eflag = reinterpret_cast<int*>(tmem_slot + 1);  // [4] epilogue warps' wait results
+  int* eflag = reinterpret_cast<int*>(tmem_slot + 1);  // [8] epilogue warps' wait results
   float* S = reinterpret_cast<float*>(smem + PCfg::kStagingOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -723,7 +726,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tc_persistent(const __grid_c
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 128);
+      mbar_init(&acce[b], 256);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -805,17 +808,21 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tc_persistent(const __grid_c
       int pi, m_tile, n_tile, split, kb0, nkb;
       gemm_tile_coords(p, tile, pi, m_tile, n_tile, split, kb0, nkb);
       const int b = ti & 1;
-      // one waiter per warp; the four warps agree before they leave together
+      // one waiter per warp; the eight warps agree before they leave together
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&accf[b], (uint32_t)(ti >> 1) & 1u, p.err, 25);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (lane == 0) eflag[warp - 2] = ok ? 1 : 0;
-      named_barrier_sync(2, 128);
-      const bool all_ok = eflag[0] && eflag[1] && eflag[2] && eflag[3];
-      named_barrier_sync(2, 128);
+      named_barrier_sync(3, 256);
+      bool all_ok = true;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) all_ok = all_ok && eflag[w];
+      named_barrier_sync(3, 256);
       if (!all_ok) break;
       tc_fence_after();
-      tc_epilogue_p(p.prob[pi], S, tmem, (uint32_t)(b * kPBN), m_tile, n_tile, split);
+      const int grp = warp >= 6 ? 1 : 0;
+      tc_epilogue_p(p.prob[pi], S + grp * (PCfg::kStagingBytes / 4), tmem, (uint32_t)(b * kPBN), m_tile, n_tile, split,
+                    grp);
       tc_fence_before();
       mbar_arrive(&acce[b]);
     }
