@@ -492,6 +492,33 @@ __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
   T* __restrict__ m = reinterpret_cast<T*>(p.mean) + (size_t)bb * p.S * p.D + d;
   const float* __restrict__ div = p.div;
   const float* __restrict__ rc = p.recip;
+  if constexpr (sizeof(T) == 2) {
+    if (rc) {
+      // bf16 with the reciprocal table: input pairs as packed words, 64 tokens in flight
+      constexpr int kA = 64;
+      const uint32_t* __restrict__ x32 = reinterpret_cast<const uint32_t*>(x);
+      uint32_t* __restrict__ m32 = reinterpret_cast<uint32_t*>(m);
+      const size_t rs = (size_t)(p.D / 2);
+      for (int s0 = 0; s0 < p.S; s0 += kA) {
+        const int n = min(kA, p.S - s0);
+        uint32_t v[kA];
+#pragma unroll
+        for (int j = 0; j < kA; ++j)
+          if (j < n) v[j] = x32[(size_t)(s0 + j) * rs];
+#pragma unroll
+        for (int j = 0; j < kA; ++j)
+          if (j < n) {
+            a0 += bf2_lo(v[j]);
+            a1 += bf2_hi(v[j]);
+            const float dv = __ldg(div + s0 + j), y = __ldg(rc + s0 + j);
+            m32[(size_t)(s0 + j) * rs] = pack_bf16x2(div_rn_recip(rnd<T>(a0), dv, y), div_rn_recip(rnd<T>(a1), dv, y));
+          }
+      }
+      p.state[(size_t)bb * p.D + d] = a0;
+      p.state[(size_t)bb * p.D + d + 1] = a1;
+      return;
+    }
+  }
   for (int s0 = 0; s0 < p.S; s0 += kAhead) {
     const int n = min(kAhead, p.S - s0);
     float v0[kAhead], v1[kAhead], dv[kAhead];
