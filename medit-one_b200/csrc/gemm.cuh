@@ -571,30 +571,50 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
 // Large GEMMs (prompt ingestion, batched LinearMoE): one CTA per SM loops over the tiles
 // (tile = blockIdx.x + i * gridDim.x, the linear order above). Warp 0 streams A / B stages
 // through a kPStages-deep ring, warp 1 issues the MMAs into one of two TMEM accumulators
-// (columns [0, kPBN) and [kPBN, 2 kPBN)), and two groups of four epilogue warps (2..5, 6..9)
-// drain the other accumulator, alternate kPChunk-token chunks each through its own staging
-// tile, so a tile's epilogue runs under the next tile's main loop. Same epilogue steps and
-// rounding as tc_epilogue (no fused argmax).
+// (columns [0, kPBN) and [kPBN, 2 kPBN)), and kPGroups groups of four epilogue warps (2..5,
+// 6..9, 10..13) drain the other accumulator, taking the kPChunk-token chunks in turn, each
+// group through its own staging tile, so a tile's epilogue runs under the next tile's main
+// loop. Same epilogue steps and rounding as tc_epilogue (no fused argmax).
 constexpr int kPStages = 4;
 constexpr int kPBN = 256;
-constexpr int kPChunk = 32;  // tokens per staging pass
+constexpr int kPChunk = 16;  // tokens per staging pass
+constexpr int kPGroups = 3;  // epilogue groups of four warps
 struct PCfg {
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = kPBN * 64 * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStagingOff = kPStages * kStageBytes;
   static constexpr int kStagingBytes = kPChunk * 128 * 4;  // per epilogue group
-  static constexpr int kBarOff = kStagingOff + 2 * kStagingBytes;
+  static constexpr int kBarOff = kStagingOff + kPGroups * kStagingBytes;
   static constexpr int kSmem = kBarOff + 256 + 1024 /*align*/;
-  static constexpr int kThreads = 320;  // TMA warp, MMA warp, 2 x 4 epilogue warps
+  static constexpr int kEpiThreads = kPGroups * 128;
+  static constexpr int kThreads = 64 + kEpiThreads;  // TMA warp, MMA warp, epilogue groups
 };
 static_assert(PCfg::kSmem <= 227 * 1024, "persistent GEMM shared memory");
 
-// One tile's epilogue by one group of four warps (grp 0: warps 2..5, grp 1: warps 6..9;
+constexpr int kPKU = kPChunk / 8;  // (token, 8-row) units per thread per chunk (128 threads a group)
+
+// The activation operand (hx / mean) of this thread's units in the chunk at token cc of the
+// tile: issued one chunk ahead of its use, so its latency hides under the current chunk.
+ONE_DEVINL void epi_aux_load(const GemmProblem& P, int m_tile, int n_tile, int cc, int e, uint4 (&aux)[kPKU]) {
+  using T = __nv_bfloat16;
+  const int n0 = m_tile * 128 + (e & 15) * 8;
+  const bool use = (P.kind == EPI_HXPRE || P.kind == EPI_XMOE) && n0 < P.Nw && cc < kPBN;
+#pragma unroll
+  for (int k = 0; k < kPKU; ++k) {
+    const int t = n_tile * kPBN + cc + (e >> 4) + 8 * k;
+    aux[k] = make_uint4(0, 0, 0, 0);
+    if (use && t < P.T) aux[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0);
+  }
+}
+
+// One tile's epilogue by one group of four warps (group grp: warps 2 + 4 grp .. 5 + 4 grp;
 // e = 0..127 within the group): TMEM quarter q = warp % 4, accumulator columns
-// [col0, col0 + kPBN); the group takes the chunks cc = (2 j + grp) * kPChunk, staged through S.
+// [col0, col0 + kPBN); the group takes the chunks cc = (kPGroups j + grp) * kPChunk, staged
+// through S.
+// aux holds the operands of the group's first chunk (epi_aux_load, issued by the caller).
 ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uint32_t col0, int m_tile, int n_tile,
-                              int split, int grp) {
+                              int split, int grp, uint4 (&aux)[kPKU]) {
   using T = __nv_bfloat16;
   constexpr int CH = kPChunk, NT = 128;
   constexpr int TU = NT / 16, TG = NT / 8;  // tokens per pass: (token, 8-row) / gelu units
@@ -615,17 +635,14 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
     load8(reinterpret_cast<const T*>(P.bias) + ng, bg);
     load8(reinterpret_cast<const T*>(P.bias) + ng + 8, bg + 8);
   }
-  for (int cc = grp * CH; cc < kPBN; cc += 2 * CH) {
+  static_assert(KU == kPKU, "aux prefetch shape");
+  for (int cc = grp * CH; cc < kPBN; cc += kPGroups * CH) {
     const int tn = min(CH, P.T - (t_tile + cc));
     if (tn <= 0) break;
     uint4 auxr[KU];
 #pragma unroll
-    for (int k = 0; k < KU; ++k) {
-      const int t = t_tile + cc + (e >> 4) + TU * k;
-      auxr[k] = make_uint4(0, 0, 0, 0);
-      if (aux_kind && v8 && t < P.T)
-        auxr[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0);
-    }
+    for (int k = 0; k < KU; ++k) auxr[k] = aux[k];
+    if (aux_kind) epi_aux_load(P, m_tile, n_tile, cc + kPGroups * CH, e, aux);  // next chunk
     // ---- E1: this warp's TMEM lane quarter -> S[token][row]
 #pragma unroll
     for (int c0 = 0; c0 < CH; c0 += 16) {
@@ -707,7 +724,7 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
   }
 }
 
-__global__ void __launch_bounds__(320, 1) gemm_bf16_tc_persistent(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(PCfg::kThreads, 1) gemm_bf16_tc_persistent(const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + PCfg::kBarOff);
@@ -716,7 +733,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bf16_tc_persistent(const __grid_c
   uint64_t* acce = accf + 2;          // [2] accumulator b drained by the epilogue
   uint64_t* drain = acce + 2;         // the MMA thread's last commit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  int* eflag = reinterpret_cast<int*>(tmem_slot + 1);  // [8] epilogue warps' wait results
+  int* eflag = reinterpret_cast<int*>(tmem_slot + 1);  // [4 kPGroups] epilogue warps' wait results
   float* S = reinterpret_cast<float*>(smem + PCfg::kStagingOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -726,7 +743,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bf16_tc_persistent(const __grid_c
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 256);
+      mbar_init(&acce[b], PCfg::kEpiThreads);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -808,21 +825,24 @@ __global__ void __launch_bounds__(320, 1) gemm_bf16_tc_persistent(const __grid_c
       int pi, m_tile, n_tile, split, kb0, nkb;
       gemm_tile_coords(p, tile, pi, m_tile, n_tile, split, kb0, nkb);
       const int b = ti & 1;
-      // one waiter per warp; the eight warps agree before they leave together
+      // the first chunk's activation operands are requested before the accumulator wait
+      const int grp = (warp - 2) >> 2;
+      uint4 aux[kPKU];
+      epi_aux_load(p.prob[pi], m_tile, n_tile, grp * kPChunk, threadIdx.x - 64 - 128 * grp, aux);
+      // one waiter per warp; the epilogue warps agree before they leave together
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&accf[b], (uint32_t)(ti >> 1) & 1u, p.err, 25);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (lane == 0) eflag[warp - 2] = ok ? 1 : 0;
-      named_barrier_sync(3, 256);
+      named_barrier_sync(1 + kPGroups, PCfg::kEpiThreads);
       bool all_ok = true;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) all_ok = all_ok && eflag[w];
-      named_barrier_sync(3, 256);
+      for (int w = 0; w < 4 * kPGroups; ++w) all_ok = all_ok && eflag[w];
+      named_barrier_sync(1 + kPGroups, PCfg::kEpiThreads);
       if (!all_ok) break;
       tc_fence_after();
-      const int grp = warp >= 6 ? 1 : 0;
       tc_epilogue_p(p.prob[pi], S + grp * (PCfg::kStagingBytes / 4), tmem, (uint32_t)(b * kPBN), m_tile, n_tile, split,
-                    grp);
+                    grp, aux);
       tc_fence_before();
       mbar_arrive(&acce[b]);
     }
