@@ -277,6 +277,34 @@ struct TcCfg {
 //       S[token][row] (the drained pipeline buffers), kChunk tokens at a time.
 //   E2: unit = (token, 8 consecutive rows) [GELU_UP: (token, 8 outputs from 16 rows)];
 //       thread e owns the row slice e % 16 (e % 8) of every 12th (24th) token; 16-byte stores.
+// Epilogue of 8 consecutive outputs of one token on packed bf16x2 pairs (a = accumulator +
+// bias, fp32): y = rnd(a); CX stores y and clamp(y, +-bf16(1e4)); HXPRE stores
+// rnd(aux + clamp(y, +-100)), XMOE rnd(aux * clamp(y, +-100)). The bounds are bf16 values and
+// each packed add / multiply of bf16 operands is one rounding of the exact result, so the
+// values equal the fp32-then-round sequence of one/modeling_one.py:559-565 and
+// one/linear_moe.py:53.
+ONE_DEVINL void epi_packed8(int kind, const float (&a)[8], const uint4& aux, __nv_bfloat16* out, __nv_bfloat16* out2) {
+  uint32_t y[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) y[j] = pack_bf16x2(a[2 * j], a[2 * j + 1]);
+  if (kind == EPI_CX) {
+    *reinterpret_cast<uint4*>(out) = make_uint4(y[0], y[1], y[2], y[3]);
+    uint32_t z[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) z[j] = bf2_min(bf2_max(y[j], 0xc61cc61cu), 0x461c461cu);  // +-9984
+    *reinterpret_cast<uint4*>(out2) = make_uint4(z[0], z[1], z[2], z[3]);
+    return;
+  }
+  const uint32_t x[4] = {aux.x, aux.y, aux.z, aux.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t cl = bf2_min(bf2_max(y[j], 0xc2c8c2c8u), 0x42c842c8u);  // +-100
+    o[j] = kind == EPI_HXPRE ? bf2_add(x[j], cl) : bf2_mul(x[j], cl);
+  }
+  *reinterpret_cast<uint4*>(out) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 template <int BN>
 __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProblem& P, float* S, uint32_t tmem,
                                             uint64_t* accb, int m_tile, int n_tile, int split) {
@@ -416,30 +444,8 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
         T* out = reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n0;
         if (kind == EPI_STORE) {
           store8(out, a);
-        } else if (kind == EPI_CX) {
-          float y[8], z[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            y[j] = rnd<T>(a[j]);
-            z[j] = fminf(fmaxf(y[j], -1e4f), 1e4f);
-          }
-          store8(out, y);
-          store8(reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0, z);
-        } else {  // HXPRE: aux + clamp(y); XMOE: aux * clamp(y)
-          float x[8], y[8];
-          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&auxr[k]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(h2[j]);
-            x[2 * j] = f.x;
-            x[2 * j + 1] = f.y;
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float cl = fminf(fmaxf(rnd<T>(a[j]), -100.f), 100.f);
-            y[j] = kind == EPI_HXPRE ? x[j] + cl : x[j] * cl;
-          }
-          store8(out, y);
+        } else {
+          epi_packed8(kind, a, auxr[k], out, reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0);
         }
       }
     }
@@ -693,30 +699,8 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
         T* out = reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n0;
         if (kind == EPI_STORE) {
           store8(out, a);
-        } else if (kind == EPI_CX) {
-          float y[8], z[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            y[j] = rnd<T>(a[j]);
-            z[j] = fminf(fmaxf(y[j], -1e4f), 1e4f);
-          }
-          store8(out, y);
-          store8(reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0, z);
-        } else {  // HXPRE: aux + clamp(y); XMOE: aux * clamp(y)
-          float x[8], y[8];
-          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&auxr[k]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(h2[j]);
-            x[2 * j] = f.x;
-            x[2 * j + 1] = f.y;
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float cl = fminf(fmaxf(rnd<T>(a[j]), -100.f), 100.f);
-            y[j] = kind == EPI_HXPRE ? x[j] + cl : x[j] * cl;
-          }
-          store8(out, y);
+        } else {
+          epi_packed8(kind, a, auxr[k], out, reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0);
         }
       }
     }
