@@ -201,9 +201,9 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     cfg = config_140m()
-    # bounded sample: each CPU step of 256 sequences takes ~0.5 s; cap the run
-    steps = max(1, min(args.steps, 8))
-    warmup = max(0, min(args.warmup, 2))
+    # bounded sample: a CPU step of 256 sequences takes ~0.1-0.5 s on the host; cap the run
+    steps = max(1, min(args.steps, 30))
+    warmup = max(0, min(args.warmup, 5))
     r = cpu_reference(cfg, steps, warmup, BATCH, PROMPT)
     line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": args.gpus,
             "steps": steps, "warmup": warmup, "ms_per_step": 1000 * r["seconds"] / steps, "higher_is_better": True,
