@@ -414,14 +414,15 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
         const int tl = (e >> 3) + TG * k;
         if (tl >= tn || ng >= P.Nw) continue;
         const float* sv = S + tl * 128 + cg * 16;
-        float o8[8];
+        // gelu(g) * u on packed pairs: g, u and gelu(g) rounded to bf16, one rounded product
+        uint32_t o4[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float gb = rnd<T>(sv[2 * j] + bg[2 * j]);
-          const float ub = rnd<T>(sv[2 * j + 1] + bg[2 * j + 1]);
-          o8[j] = rnd<T>(gelu_erf(gb)) * ub;
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t g2 = pack_bf16x2(sv[4 * j] + bg[4 * j], sv[4 * j + 2] + bg[4 * j + 2]);
+          const uint32_t u2 = pack_bf16x2(sv[4 * j + 1] + bg[4 * j + 1], sv[4 * j + 3] + bg[4 * j + 3]);
+          o4[j] = bf2_mul(pack_bf16x2(gelu_erf(bf2_lo(g2)), gelu_erf(bf2_hi(g2))), u2);
         }
-        store8(out + (size_t)(tb + tl) * P.ldo + (ng >> 1), o8);
+        *reinterpret_cast<uint4*>(out + (size_t)(tb + tl) * P.ldo + (ng >> 1)) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
       }
     } else {
 #pragma unroll
@@ -669,14 +670,15 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
         const int tl = (e >> 3) + TG * k;
         if (tl >= tn || ng >= P.Nw) continue;
         const float* sv = S + tl * 128 + cg * 16;
-        float o8[8];
+        // gelu(g) * u on packed pairs: g, u and gelu(g) rounded to bf16, one rounded product
+        uint32_t o4[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float gb = rnd<T>(sv[2 * j] + bg[2 * j]);
-          const float ub = rnd<T>(sv[2 * j + 1] + bg[2 * j + 1]);
-          o8[j] = rnd<T>(gelu_erf(gb)) * ub;
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t g2 = pack_bf16x2(sv[4 * j] + bg[4 * j], sv[4 * j + 2] + bg[4 * j + 2]);
+          const uint32_t u2 = pack_bf16x2(sv[4 * j + 1] + bg[4 * j + 1], sv[4 * j + 3] + bg[4 * j + 3]);
+          o4[j] = bf2_mul(pack_bf16x2(gelu_erf(bf2_lo(g2)), gelu_erf(bf2_hi(g2))), u2);
         }
-        store8(out + (size_t)(tb + tl) * P.ldo + (ng >> 1), o8);
+        *reinterpret_cast<uint4*>(out + (size_t)(tb + tl) * P.ldo + (ng >> 1)) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
       }
     } else {
 #pragma unroll
