@@ -726,6 +726,26 @@ def profile_case(args):
     print(json.dumps({"profile_case": "ok", "launches_per_step": eng.step_launches(BATCH)}))
 
 
+def profile_prefill(args):
+    """Small fixed prompt-ingestion case for ncu captures: 140M engine, one call of 20 prompts of
+    4096 tokens, the smallest prompt set whose GEMMs take the persistent path (>= 2 tiles per SM).
+    Launch order per layer: row_pre, scan, GEMM A, attention, gate GEMM, 3 routers, x_moe GEMM,
+    gate/up GEMM, down GEMM (persistent GEMMs 0..4 of layer 0)."""
+    from one.configuration_one import config_140m
+    from one.engine import OneEngine
+    from one.initialization import init_state_dict
+    cfg = config_140m()
+    b, s = 20, 4096
+    eng = OneEngine(cfg, init_state_dict(cfg, SEED, torch.bfloat16), "cuda", torch.bfloat16, max_batch=b,
+                    max_tokens=b * s)
+    g = torch.Generator().manual_seed(PF_SEED)
+    eng.prefill(torch.randint(0, cfg.vocab_size, (b, s), generator=g).cuda())
+    torch.cuda.synchronize()
+    if eng.device_error() != (0, 0):
+        raise RuntimeError(f"device error {eng.device_error()}")
+    print(json.dumps({"profile_prefill": "ok", "tokens": b * s, "launches": eng.prefill_launches(b, s)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -734,10 +754,14 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
+    ap.add_argument("--profile-prefill", action="store_true", help="run the small prompt-ingestion ncu case and exit")
     ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe", "prefill"],
                     help="decode: the 140M decode step (default); attention: the isolated RoPE + attention op; "
                          "linear_moe: the isolated LinearMoE op on 16384 tokens; prefill: 64 x 4096-token prompts")
     args = ap.parse_args()
+    if args.profile_prefill:
+        profile_prefill(args)
+        return
     if args.profile_case:
         profile_case(args)
         return
