@@ -347,7 +347,9 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
       }
   } else {
     // finish the previous layer (:571-573, :793, :563-564); split-K partials added in order
-    float hp[NV][8];
+    // the first down_proj partial is requested with the other rows (one memory round trip when
+    // there is a single split, as in prompt ingestion)
+    float hp[NV][8], m[NV][8];
 #pragma unroll
     for (int v = 0; v < NV; ++v)
       if (act[v]) {
@@ -355,12 +357,12 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
         load8(reinterpret_cast<const T*>(p.out0) + off, a[v]);
         load8(reinterpret_cast<const T*>(p.h) + off, h[v]);
         load8(reinterpret_cast<const T*>(p.hx_pre) + off, hp[v]);
+        load8(p.ws + off, m[v]);
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) a[v][e] = h[v][e] = hp[v][e] = 0.f;
+        for (int e = 0; e < 8; ++e) a[v][e] = h[v][e] = hp[v][e] = m[v][e] = 0.f;
       }
-    float m[NV][8];
-    for (int sp = 0; sp < p.splits; ++sp) {
+    for (int sp = 1; sp < p.splits; ++sp) {
       float w[NV][8];
 #pragma unroll
       for (int v = 0; v < NV; ++v)
@@ -368,7 +370,7 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
 #pragma unroll
       for (int v = 0; v < NV; ++v)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) m[v][e] = sp == 0 ? w[v][e] : m[v][e] + w[v][e];
+        for (int e = 0; e < 8; ++e) m[v][e] += w[v][e];
     }
     float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
