@@ -44,13 +44,13 @@ struct PromptTabParams {
   int seq_len, half;    // half = 0: no RoPE table
   __nv_bfloat16* tab;   // [seq_len][2 * half]
   const float* div;     // [seq_len] prefix-mean divisors
-  float* recip;         // [seq_len] RN(1 / div)
+  float2* dr;           // [seq_len] (div, RN(1 / div))
 };
 
 __global__ void prompt_table_kernel(const PromptTabParams p) {
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < p.seq_len) p.recip[i] = 1.0f / p.div[i];
+  if (i < p.seq_len) p.dr[i] = make_float2(p.div[i], 1.0f / p.div[i]);
   if (i >= p.seq_len * p.half) return;
   const int s = i / p.half, j = i % p.half;
   const float f = p.inv_freq[j] * (float)(p.counters[0] + s);

@@ -582,7 +582,7 @@ struct Bufs {
   size_t ridx;     // i32 [Tm, 3, k]
   size_t ghx, gx;  // [Tm, r] hx_moe / x_moe gate logits (prompt ingestion)
   size_t rope;     // bf16 [Tm, head_dim] RoPE cos | sin table of a prompt call
-  size_t recip;    // fp32 [Tm] reciprocals of a prompt call's prefix-mean divisors
+  size_t recip;    // fp32 [Tm][2] a prompt call's prefix-mean divisors and their reciprocals
   size_t total;
   int ws_rows;
 };
@@ -628,7 +628,7 @@ static Bufs layout(const one_config& c, int max_tokens, int max_batch, int hist_
   b.ghx = Lo.take(Tm * (size_t)std::max(c.r, 1) * es);
   b.gx = Lo.take(Tm * (size_t)std::max(c.r, 1) * es);
   b.rope = Lo.take(Tm * (size_t)c.head_dim * 2);
-  b.recip = Lo.take(Tm * 4);
+  b.recip = Lo.take(Tm * 8);
   b.total = Lo.take(0) + 1024;
   return b;
 }
@@ -808,7 +808,7 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
     const int half = tok ? Dh / 2 : 0;
     pt.grid = (seq_len * std::max(half, 1) + 255) / 256;
     pt.pt = PromptTabParams{counters, e->inv_freq, seq_len, half, e->at<__nv_bfloat16>(e->b.rope), prompt_div,
-                            e->at<float>(e->b.recip)};
+                            e->at<float2>(e->b.recip)};
     plan.push_back(pt);
   }
   for (int l = 0; l < c.num_hidden_layers; ++l) {
@@ -862,7 +862,7 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       s.grid = (batch * (D / 2) + 127) / 128;  // one thread per (sequence, feature pair)
       s.sc = ScanParams{batch, seq_len, D, B_(e->b.norm_x), B_(e->b.mean),
                         e->at<float>(e->b.state) + (size_t)l * e->max_batch * D, prompt_div,
-                        recip ? e->at<float>(e->b.recip) : nullptr};
+                        recip ? e->at<float2>(e->b.recip) : nullptr};
       plan.push_back(s);
     }
     // ---- gemm A

@@ -447,7 +447,7 @@ struct ScanParams {
   void* mean;           // [B, S, D]
   float* state;         // [B, D] running sum in / out (decode state after the prompt)
   const float* div;     // [S] divisor of each prompt position
-  const float* recip;   // [S] 1 / div rounded to nearest (bf16 models), or null
+  const float2* dr;     // [S] (div, RN(1 / div)) of each prompt position (bf16 models), or null
 };
 
 // a / b rounded to nearest-even in fp32, given y = RN(1 / b), by one residual correction
@@ -493,28 +493,34 @@ __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
   const T* __restrict__ x = reinterpret_cast<const T*>(p.norm_x) + (size_t)bb * p.S * p.D + d;
   T* __restrict__ m = reinterpret_cast<T*>(p.mean) + (size_t)bb * p.S * p.D + d;
   const float* __restrict__ div = p.div;
-  const float* __restrict__ rc = p.recip;
   if constexpr (sizeof(T) == 2) {
-    if (rc) {
-      // bf16 with the reciprocal table: input pairs as packed words, 64 tokens in flight
-      constexpr int kA = 64;
+    if (p.dr) {
+      // bf16 with the (divisor, reciprocal) table: input pairs as packed words; the next 32
+      // tokens' loads are in flight while the current 32 are summed and divided
+      constexpr int kA = 32;
       const uint32_t* __restrict__ x32 = reinterpret_cast<const uint32_t*>(x);
       uint32_t* __restrict__ m32 = reinterpret_cast<uint32_t*>(m);
+      const float2* __restrict__ dr = p.dr;
       const size_t rs = (size_t)(p.D / 2);
+      uint32_t vc[kA], vn[kA];
+#pragma unroll
+      for (int j = 0; j < kA; ++j)
+        if (j < p.S) vc[j] = x32[(size_t)j * rs];
       for (int s0 = 0; s0 < p.S; s0 += kA) {
-        const int n = min(kA, p.S - s0);
-        uint32_t v[kA];
+        const int n = min(kA, p.S - s0), nn = min(kA, p.S - s0 - kA);
 #pragma unroll
         for (int j = 0; j < kA; ++j)
-          if (j < n) v[j] = x32[(size_t)(s0 + j) * rs];
+          if (j < nn) vn[j] = x32[(size_t)(s0 + kA + j) * rs];
 #pragma unroll
         for (int j = 0; j < kA; ++j)
           if (j < n) {
-            a0 += bf2_lo(v[j]);
-            a1 += bf2_hi(v[j]);
-            const float dv = __ldg(div + s0 + j), y = __ldg(rc + s0 + j);
-            m32[(size_t)(s0 + j) * rs] = pack_bf16x2(div_rn_recip(rnd<T>(a0), dv, y), div_rn_recip(rnd<T>(a1), dv, y));
+            a0 += bf2_lo(vc[j]);
+            a1 += bf2_hi(vc[j]);
+            const float2 q = __ldg(dr + s0 + j);
+            m32[(size_t)(s0 + j) * rs] = pack_bf16x2(div_rn_recip(rnd<T>(a0), q.x, q.y), div_rn_recip(rnd<T>(a1), q.x, q.y));
           }
+#pragma unroll
+        for (int j = 0; j < kA; ++j) vc[j] = vn[j];
       }
       p.state[(size_t)bb * p.D + d] = a0;
       p.state[(size_t)bb * p.D + d + 1] = a1;
@@ -530,27 +536,13 @@ __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
         ld2(x + (size_t)(s0 + j) * p.D, v0[j], v1[j]);
         dv[j] = __ldg(div + s0 + j);
       }
-    if (rc) {
-      float y[kAhead];
 #pragma unroll
-      for (int j = 0; j < kAhead; ++j)
-        if (j < n) y[j] = __ldg(rc + s0 + j);
-#pragma unroll
-      for (int j = 0; j < kAhead; ++j)
-        if (j < n) {
-          a0 += v0[j];
-          a1 += v1[j];
-          st2(m + (size_t)(s0 + j) * p.D, div_rn_recip(rnd<T>(a0), dv[j], y[j]), div_rn_recip(rnd<T>(a1), dv[j], y[j]));
-        }
-    } else {
-#pragma unroll
-      for (int j = 0; j < kAhead; ++j)
-        if (j < n) {
-          a0 += v0[j];
-          a1 += v1[j];
-          st2(m + (size_t)(s0 + j) * p.D, rnd<T>(a0) / dv[j], rnd<T>(a1) / dv[j]);
-        }
-    }
+    for (int j = 0; j < kAhead; ++j)
+      if (j < n) {
+        a0 += v0[j];
+        a1 += v1[j];
+        st2(m + (size_t)(s0 + j) * p.D, rnd<T>(a0) / dv[j], rnd<T>(a1) / dv[j]);
+      }
   }
   p.state[(size_t)bb * p.D + d] = a0;
   p.state[(size_t)bb * p.D + d + 1] = a1;
