@@ -216,6 +216,20 @@ ONE_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, DevErr* err, int where
   }
 }
 
+// ------------------------------------------------------------------ cp.async (global -> shared)
+ONE_DEVINL void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+ONE_DEVINL void cp_async8(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+ONE_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// waits until at most N of this thread's committed groups are still in flight
+template <int N>
+ONE_DEVINL void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ------------------------------------------------------------------ TMA (no cluster forms)
 ONE_DEVINL void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -355,6 +355,7 @@ static int set_kernel_attrs() {
   }
   CK(cudaFuncSetAttribute(dec_attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(dec_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaFuncSetAttribute(scan_mean_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem));
   CK(cudaFuncSetAttribute(attn_tok_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<32>::total(16)));
   CK(cudaFuncSetAttribute(attn_tok_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTokSmem<64>::total(16)));
   g_attrs_set = true;
@@ -431,6 +432,10 @@ static int run(const Launch& L, cudaStream_t st) {
                : launch_k(row_attn_kernel<float, 64>, dim3(L.grid), dim3(L.block), L.smem, st, L.ra);
       break;
     case L_SCAN:
+      if (L.nv == 2) {
+        e = launch_k(scan_mean_staged_kernel, dim3(L.grid), dim3(L.block), L.smem, st, L.sc);
+        break;
+      }
       e = bf ? launch_k(scan_mean_kernel<__nv_bfloat16>, dim3(L.grid), dim3(L.block), 0, st, L.sc)
              : launch_k(scan_mean_kernel<float>, dim3(L.grid), dim3(L.block), 0, st, L.sc);
       break;
@@ -863,6 +868,13 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       s.sc = ScanParams{batch, seq_len, D, B_(e->b.norm_x), B_(e->b.mean),
                         e->at<float>(e->b.state) + (size_t)l * e->max_batch * D, prompt_div,
                         recip ? e->at<float2>(e->b.recip) : nullptr};
+      if (recip && dt == ONE_DTYPE_BF16 && D % kScanFeat == 0) {
+        // staged through shared memory: a CTA per (sequence, 128 features)  (nv = 2)
+        s.nv = 2;
+        s.block = kScanThreads;
+        s.grid = batch * (D / kScanFeat);
+        s.smem = kScanSmem;
+      }
       plan.push_back(s);
     }
     // ---- gemm A
