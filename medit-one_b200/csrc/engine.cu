@@ -1084,6 +1084,17 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       Launch g;
       int rc = plan_gemm(g, ps, 1, T, dt, err);
       if (rc) return rc;
+      GemmProblem& P = g.g.prob[0];
+      if (g.kind == L_GEMM_TC && g.persist && P.splits == 1) {
+        // unsplit (prompt ingestion): the epilogue adds the down bias and the residual out0
+        // in place, so the next row_pre reads one bf16 row instead of an fp32 partial
+        P.kind = EPI_RESID;
+        P.bias = c.mlp_bias ? LW(ONE_W_DOWN_B) : nullptr;
+        P.aux = B_(e->b.out0);
+        P.lda = D;
+        P.out = B_(e->b.out0);
+        P.ldo = D;
+      }
       plan.push_back(g);
     }
   }
@@ -1108,6 +1119,7 @@ static int build_final(one_engine* e, std::vector<Launch>& plan, int T, int batc
     if (it->kind == L_GEMM_TC || it->kind == L_GEMM_SIMT) {
       const GemmProblem& P = it->kind == L_GEMM_TC ? it->g.prob[0] : it->sg.prob[0];
       if (P.kind == EPI_PARTIAL) splits = P.splits;
+      if (P.kind == EPI_RESID) splits = 0;
       break;
     }
   Launch rp;
@@ -1183,6 +1195,7 @@ static void link_splits(std::vector<Launch>& plan) {
     if (L.kind == L_GEMM_TC || L.kind == L_GEMM_SIMT) {
       const GemmProblem& P = L.kind == L_GEMM_TC ? L.g.prob[0] : L.sg.prob[0];
       if (P.kind == EPI_PARTIAL) splits = P.splits;
+      if (P.kind == EPI_RESID) splits = 0;
     } else if (L.kind == L_ROW_PRE || L.kind == L_ROW_PRE_W) {
       L.rp.splits = splits;
     }

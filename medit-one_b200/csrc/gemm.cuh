@@ -23,6 +23,8 @@ enum EpiKind : int {
   EPI_GELU_UP = 4,  // rows interleaved (gate j, up j): out[j] = rnd(rnd(gelu(g)) * u)  (OneMLP, :205-206)
   EPI_PARTIAL = 5,  // fp32 split-K partial: ws[split][t][n] = acc
   EPI_ARGMAX = 6,   // logits v = rnd(acc): per-token (max v, lowest n) by 64-bit atomicMax
+  EPI_RESID = 7,    // out = rnd(aux + rnd(acc + bias)), bf16, persistent kernel only: the MLP
+                    // residual out0 + down_proj(...) (:571) of an unsplit down_proj, in place
 };
 
 constexpr int kMaxProblems = 4;
@@ -279,7 +281,7 @@ struct TcCfg {
 //       thread e owns the row slice e % 16 (e % 8) of every 12th (24th) token; 16-byte stores.
 // Epilogue of 8 consecutive outputs of one token on packed bf16x2 pairs (a = accumulator +
 // bias, fp32): y = rnd(a); CX stores y and clamp(y, +-bf16(1e4)); HXPRE stores
-// rnd(aux + clamp(y, +-100)), XMOE rnd(aux * clamp(y, +-100)). The bounds are bf16 values and
+// rnd(aux + clamp(y, +-100)), XMOE rnd(aux * clamp(y, +-100)), RESID rnd(aux + y). The bounds are bf16 values and
 // each packed add / multiply of bf16 operands is one rounding of the exact result, so the
 // values equal the fp32-then-round sequence of one/modeling_one.py:559-565 and
 // one/linear_moe.py:53.
@@ -297,6 +299,12 @@ ONE_DEVINL void epi_packed8(int kind, const float (&a)[8], const uint4& aux, __n
   }
   const uint32_t x[4] = {aux.x, aux.y, aux.z, aux.w};
   uint32_t o[4];
+  if (kind == EPI_RESID) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = bf2_add(x[j], y[j]);
+    *reinterpret_cast<uint4*>(out) = make_uint4(o[0], o[1], o[2], o[3]);
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t cl = bf2_min(bf2_max(y[j], 0xc2c8c2c8u), 0x42c842c8u);  // +-100
@@ -606,7 +614,7 @@ constexpr int kPKU = kPChunk / 8;  // (token, 8-row) units per thread per chunk 
 ONE_DEVINL void epi_aux_load(const GemmProblem& P, int m_tile, int n_tile, int cc, int e, uint4 (&aux)[kPKU]) {
   using T = __nv_bfloat16;
   const int n0 = m_tile * 128 + (e & 15) * 8;
-  const bool use = (P.kind == EPI_HXPRE || P.kind == EPI_XMOE) && n0 < P.Nw && cc < kPBN;
+  const bool use = (P.kind == EPI_HXPRE || P.kind == EPI_XMOE || P.kind == EPI_RESID) && n0 < P.Nw && cc < kPBN;
 #pragma unroll
   for (int k = 0; k < kPKU; ++k) {
     const int t = n_tile * kPBN + cc + (e >> 4) + 8 * k;
@@ -631,7 +639,7 @@ ONE_DEVINL void tc_epilogue_p(const GemmProblem& P, float* S, uint32_t tmem, uin
   const int bar = 1 + grp;
   const int n_base = m_tile * 128, t_tile = n_tile * kPBN;
   const int kind = P.kind;
-  const bool aux_kind = kind == EPI_HXPRE || kind == EPI_XMOE;
+  const bool aux_kind = kind == EPI_HXPRE || kind == EPI_XMOE || kind == EPI_RESID;
   const int c8 = e & 15, n0 = n_base + c8 * 8;
   const bool v8 = n0 < P.Nw;
   float b8[8] = {0, 0, 0, 0, 0, 0, 0, 0};

@@ -81,7 +81,7 @@ struct RowPreParams {
   int div_len;
   // previous layer's tail
   const float* ws;        // [splits][T][D] down_proj partials
-  int splits;
+  int splits;             // 0: out0 already holds out0 + down_proj(...) (EPI_RESID)
   const void* down_b;     // down_proj bias (mlp_bias) or null
   const void* out0;       // [T, D] mean * x_moe (the MLP input)
   const void* hx_pre;     // [T, D] hx + hx_moe, before norm
@@ -227,6 +227,7 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
       load8(reinterpret_cast<const T*>(p.out0) + off, a);
       load8(reinterpret_cast<const T*>(p.h) + off, h);
       load8(reinterpret_cast<const T*>(p.hx_pre) + off, hp);
+      // splits == 0: the down_proj epilogue already stored out0 + down_proj(...) in out0
       for (int s0 = 0; s0 < p.splits; s0 += 8) {
         float v[8][8];
 #pragma unroll
@@ -239,11 +240,13 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
             for (int e = 0; e < 8; ++e) m[e] = (s0 + j == 0) ? v[j][e] : m[e] + v[j][e];
           }
       }
-      if (p.down_b)
+      if (p.splits > 0) {
+        if (p.down_b)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) m[e] += db[e];
+          for (int e = 0; e < 8; ++e) m[e] += db[e];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) a[e] = rnd<T>(a[e] + rnd<T>(m[e]));
+        for (int e = 0; e < 8; ++e) a[e] = rnd<T>(a[e] + rnd<T>(m[e]));
+      }
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) a[e] = h[e] = hp[e] = 0.f;
@@ -357,7 +360,7 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
         load8(reinterpret_cast<const T*>(p.out0) + off, a[v]);
         load8(reinterpret_cast<const T*>(p.h) + off, h[v]);
         load8(reinterpret_cast<const T*>(p.hx_pre) + off, hp[v]);
-        load8(p.ws + off, m[v]);
+        if (p.splits > 0) load8(p.ws + off, m[v]);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) a[v][e] = h[v][e] = hp[v][e] = m[v][e] = 0.f;
@@ -376,14 +379,16 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
 #pragma unroll
     for (int v = 0; v < NV; ++v)
       if (act[v]) {
-        if (p.down_b) {
-          float db[8];
-          load8(reinterpret_cast<const T*>(p.down_b) + (lane + 32 * v) * 8, db);
+        if (p.splits > 0) {  // splits == 0: out0 already holds out0 + down_proj(...)
+          if (p.down_b) {
+            float db[8];
+            load8(reinterpret_cast<const T*>(p.down_b) + (lane + 32 * v) * 8, db);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) m[v][e] += db[e];
+            for (int e = 0; e < 8; ++e) m[v][e] += db[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[v][e] = rnd<T>(a[v][e] + rnd<T>(m[v][e]));
         }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a[v][e] = rnd<T>(a[v][e] + rnd<T>(m[v][e]));
         ss0 += sumsq8(a[v]);
         ss1 += sumsq8(hp[v]);
       }

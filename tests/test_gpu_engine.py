@@ -138,6 +138,39 @@ def test_140m_prefill_matches_oracle_bf16():
     assert_close(cx.float().cpu().view(2, 96, -1).numpy(), ref.cx.float().numpy(), "bf16", "cx")
 
 
+def test_140m_long_prefill_batch_invariant_bf16():
+    """Prompt ingestion at the size that takes the long-prompt kernels (8 prompts x 2048 tokens:
+    persistent GEMMs, the residual added in the unsplit down_proj epilogue, the prefix mean
+    staged over 32 tiles) against the same prompts ingested one at a time (split-K down_proj,
+    the partials added by row_pre), a path the 2 x 96 oracle test pins. Each prompt's
+    last-position logits, the last layer's hx / cx and the running sums agree."""
+    from one.configuration_one import config_140m
+    from one.initialization import init_state_dict
+    cfg = config_140m()
+    sd = init_state_dict(cfg, 7, torch.bfloat16)
+    B, S = 8, 2048
+    ids = torch.randint(0, 32000, (B, S), generator=torch.Generator().manual_seed(7))
+    big = make_engine(cfg, sd, "bf16", max_batch=B, max_tokens=B * S)
+    lg = big.prefill(ids.cuda(), logits="last").float().cpu()
+    torch.cuda.synchronize()
+    assert big.device_error() == (0, 0)
+    hx, cx = big.last_hx_cx(B * S)
+    hx, cx = hx.float().cpu().view(B, S, -1), cx.float().cpu().view(B, S, -1)
+    st = big.state()[:, :B].cpu()
+    del big
+    one = make_engine(cfg, sd, "bf16", max_batch=1, max_tokens=S)
+    for b in (0, 5):
+        lg1 = one.prefill(ids[b:b + 1].cuda(), logits="last").float().cpu()
+        torch.cuda.synchronize()
+        assert one.device_error() == (0, 0)
+        assert_close(lg[b].numpy(), lg1[0].numpy(), "bf16", f"prompt {b} logits")
+        h1, c1 = one.last_hx_cx(S)
+        assert_close(hx[b].numpy(), h1.float().cpu().numpy(), "bf16", f"prompt {b} hx")
+        assert_close(cx[b].numpy(), c1.float().cpu().numpy(), "bf16", f"prompt {b} cx")
+        s1 = one.state()[:, 0].cpu()
+        assert_close(st[:, b].numpy() / S, s1.numpy() / S, "bf16", f"prompt {b} running mean")
+
+
 def routing_heavy(sd, seed):
     """The LinearMoE tensors of a random-init state dict redrawn so that routing depends on the
     token: experts ~ N(0, 30) (distinct factors 1 + silu(score)), bias2 = 0 (a bias would fix
