@@ -443,6 +443,94 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
     }
 }
 
+// row_pre_warp_kernel's PRE_MID step for bf16 after an unsplit down_proj (splits == 0: out0
+// already holds out0 + down_proj(...)). The three input rows stay packed bf16 in registers
+// until each step unpacks the chunk it needs, so six CTAs (24 warps) fit an SM instead of
+// three. Same steps, rounding and summation order as row_pre_warp_kernel: bit-identical.
+ONE_DEVINL void unpack8(const uint4& u, float* v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf2_lo(w[i]);
+    v[2 * i + 1] = bf2_hi(w[i]);
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(128, NV <= 3 ? 6 : 5) row_pre_resid_kernel(const RowPreParams p) {
+  using T = __nv_bfloat16;
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait();
+  if (t >= p.T) return;
+  const int D = p.D, nch = D / 8;
+  const size_t row = (size_t)t * D;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  uint4 ua[NV], uh[NV], up[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const size_t off = row + (size_t)(lane + 32 * v) * 8;
+    const bool act = lane + 32 * v < nch;
+    ua[v] = act ? *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.out0) + off) : z;
+    uh[v] = act ? *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.h) + off) : z;
+    up[v] = act ? *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.hx_pre) + off) : z;
+  }
+  // out = norm(out0 + down_proj(...)) (:571-573), h += out (:793), hx = norm(hx + hx_moe) (:563-564)
+  float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+    if (lane + 32 * v < nch) {
+      float a[8], hp[8];
+      unpack8(ua[v], a);
+      unpack8(up[v], hp);
+      ss0 += sumsq8(a);
+      ss1 += sumsq8(hp);
+    }
+  ss0 = warp_sum(ss0);
+  ss1 = warp_sum(ss1);
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+    if (lane + 32 * v < nch) {
+      const int c = lane + 32 * v;
+      const size_t off = row + (size_t)c * 8;
+      float pw[8], pb[8], x[8], b[8], h[8];
+      load8(reinterpret_cast<const T*>(p.prev_norm_w) + c * 8, pw);
+      if (p.prev_norm_b) load8(reinterpret_cast<const T*>(p.prev_norm_b) + c * 8, pb);
+      unpack8(ua[v], x);
+      chunk_norm_r<T>(x, ss0, D, 1e-6f, pw, pb, p.prev_norm_b != nullptr, b);
+      unpack8(uh[v], h);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = rnd<T>(h[e] + b[e]);
+      unpack8(up[v], x);
+      chunk_norm_r<T>(x, ss1, D, 1e-6f, pw, pb, p.prev_norm_b != nullptr, b);
+      store8(reinterpret_cast<T*>(p.hx) + off, b);
+      store8(reinterpret_cast<T*>(p.h) + off, h);
+      uh[v] = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
+                         pack_bf16x2(h[6], h[7]));
+    }
+  // norm_x = norm1(h) (:340)
+  float s3 = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+    if (lane + 32 * v < nch) {
+      float h[8];
+      unpack8(uh[v], h);
+      s3 += sumsq8(h);
+    }
+  s3 = warp_sum(s3);
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+    if (lane + 32 * v < nch) {
+      const int c = lane + 32 * v;
+      float w1[8], h[8], b[8];
+      load8(reinterpret_cast<const T*>(p.norm1_w) + c * 8, w1);
+      unpack8(uh[v], h);
+      chunk_norm_r<T>(h, s3, D, 1e-6f, w1, w1, false, b);
+      store8(reinterpret_cast<T*>(p.norm_x) + row + (size_t)c * 8, b);
+    }
+}
+
 // ------------------------------------------------------------------ prefill prefix mean
 // cumsum over the sequence in fp32 (CPU cumsum accumulates in order, in fp32) divided
 // by the arange divisors (:376-387). One thread per (sequence, feature).
