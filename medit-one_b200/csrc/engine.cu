@@ -368,13 +368,13 @@ static cudaError_t launch_row_pre(const Launch& L, cudaStream_t st) {
 }
 template <typename T>
 static cudaError_t launch_row_pre_w(const Launch& L, cudaStream_t st) {
-  if (sizeof(T) == 2 && L.rp.splits == 0 && L.rp.mode == PRE_MID) {
-    // out0 already holds the MLP residual (unsplit down_proj): packed-row variant
+  if (sizeof(T) == 2 && (L.rp.mode == PRE_FIRST || L.rp.splits == 0)) {
+    // the first layer, or out0 already holds the MLP residual (unsplit down_proj): packed rows
     switch (L.nv) {
-      case 1: return launch_k(row_pre_resid_kernel<1>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
-      case 2: return launch_k(row_pre_resid_kernel<2>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
-      case 3: return launch_k(row_pre_resid_kernel<3>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
-      default: return launch_k(row_pre_resid_kernel<4>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+      case 1: return launch_k(row_pre_packed_kernel<1>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+      case 2: return launch_k(row_pre_packed_kernel<2>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+      case 3: return launch_k(row_pre_packed_kernel<3>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
+      default: return launch_k(row_pre_packed_kernel<4>, dim3(L.grid), dim3(L.block), 0, st, L.rp);
     }
   }
   switch (L.nv) {

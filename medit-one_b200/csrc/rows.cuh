@@ -300,6 +300,27 @@ __global__ void __launch_bounds__(128) row_pre_kernel(const RowPreParams p) {
 // the 8-element chunks l, l + 32, ... (NV of them), reductions by warp shuffles only (no CTA
 // barrier). Same steps and rounding as row_pre_kernel; the row sums of squares are added in
 // another order (fp32), as any reduction of the reference's norm may be.
+// PRE_FIRST, one lane per token: the token id (fed back from the argmax, or given), checked
+// against the vocabulary, recorded in ids_out / the history; clears the argmax slot.
+ONE_DEVINL int first_token_id(const RowPreParams& p, int t) {
+  int id = p.ids_from_best ? 0 : p.ids[t];
+  if (p.ids_from_best) {
+    const unsigned long long key = p.best[t];
+    id = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
+  }
+  if (id < 0 || id >= p.vocab) {  // never gather outside the embedding table
+    set_err(p.err, ERR_BAD_ARG, 100);
+    id = 0;
+  }
+  p.best[t] = 0ull;
+  if (p.ids_out) p.ids_out[t] = id;
+  if (p.hist) {
+    const int step = p.counters[1];
+    if (step < p.hist_cap) p.hist[(size_t)step * p.T + t] = id;
+  }
+  return id;
+}
+
 template <typename T, int NV>
 __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams p) {
   const int lane = threadIdx.x & 31;
@@ -315,23 +336,7 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
   float h[NV][8], a[NV][8], b[8];
   if (p.mode == PRE_FIRST) {
     int id = 0;
-    if (lane == 0) {
-      id = p.ids_from_best ? 0 : p.ids[t];
-      if (p.ids_from_best) {
-        const unsigned long long key = p.best[t];
-        id = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
-      }
-      if (id < 0 || id >= p.vocab) {  // never gather outside the embedding table
-        set_err(p.err, ERR_BAD_ARG, 100);
-        id = 0;
-      }
-      p.best[t] = 0ull;
-      if (p.ids_out) p.ids_out[t] = id;
-      if (p.hist) {
-        const int step = p.counters[1];
-        if (step < p.hist_cap) p.hist[(size_t)step * p.T + t] = id;
-      }
-    }
+    if (lane == 0) id = first_token_id(p, t);
     id = __shfl_sync(0xffffffffu, id, 0);
 #pragma unroll
     for (int v = 0; v < NV; ++v)
@@ -443,10 +448,11 @@ __global__ void __launch_bounds__(128, 3) row_pre_warp_kernel(const RowPreParams
     }
 }
 
-// row_pre_warp_kernel's PRE_MID step for bf16 after an unsplit down_proj (splits == 0: out0
-// already holds out0 + down_proj(...)). The three input rows stay packed bf16 in registers
-// until each step unpacks the chunk it needs, so six CTAs (24 warps) fit an SM instead of
-// three. Same steps, rounding and summation order as row_pre_warp_kernel: bit-identical.
+// row_pre_warp_kernel for bf16 rows at the first layer (PRE_FIRST), and at the later layers
+// and the final stage after an unsplit down_proj (splits == 0: out0 already holds
+// out0 + down_proj(...)). The input rows stay packed bf16 in registers until each step
+// unpacks the chunk it needs, so six CTAs (24 warps) fit an SM instead of three. Same steps,
+// rounding and summation order as row_pre_warp_kernel: bit-identical.
 ONE_DEVINL void unpack8(const uint4& u, float* v) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -457,7 +463,7 @@ ONE_DEVINL void unpack8(const uint4& u, float* v) {
 }
 
 template <int NV>
-__global__ void __launch_bounds__(128, NV <= 3 ? 6 : 5) row_pre_resid_kernel(const RowPreParams p) {
+__global__ void __launch_bounds__(128, NV <= 3 ? 6 : 5) row_pre_packed_kernel(const RowPreParams p) {
   using T = __nv_bfloat16;
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -467,7 +473,31 @@ __global__ void __launch_bounds__(128, NV <= 3 ? 6 : 5) row_pre_resid_kernel(con
   const int D = p.D, nch = D / 8;
   const size_t row = (size_t)t * D;
   const uint4 z = make_uint4(0, 0, 0, 0);
-  uint4 ua[NV], uh[NV], up[NV];
+  uint4 uh[NV];
+  if (p.mode == PRE_FIRST) {
+    // embedding row (:335); hx = 1, cx = h, the LinearMoE-clamped cx (+-bf16(1e4) = +-9984:
+    // the bf16 rounding of the fp32 clamp of a bf16 value)
+    int id = 0;
+    if (lane == 0) id = first_token_id(p, t);
+    id = __shfl_sync(0xffffffffu, id, 0);
+    const uint4 one = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      uh[v] = z;
+      if (lane + 32 * v < nch) {
+        const size_t off = row + (size_t)(lane + 32 * v) * 8;
+        const uint4 e = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.emb) + (size_t)id * D + (lane + 32 * v) * 8);
+        uh[v] = e;
+        const uint4 c = make_uint4(bf2_min(bf2_max(e.x, 0xc61cc61cu), 0x461c461cu), bf2_min(bf2_max(e.y, 0xc61cc61cu), 0x461c461cu),
+                                   bf2_min(bf2_max(e.z, 0xc61cc61cu), 0x461c461cu), bf2_min(bf2_max(e.w, 0xc61cc61cu), 0x461c461cu));
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.hx) + off) = one;
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.cx) + off) = e;
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.cxc) + off) = c;
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h) + off) = e;
+      }
+    }
+  } else {
+  uint4 ua[NV], up[NV];
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
     const size_t off = row + (size_t)(lane + 32 * v) * 8;
@@ -509,7 +539,8 @@ __global__ void __launch_bounds__(128, NV <= 3 ? 6 : 5) row_pre_resid_kernel(con
       uh[v] = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
                          pack_bf16x2(h[6], h[7]));
     }
-  // norm_x = norm1(h) (:340)
+  }
+  // PRE_FINAL: the lm-head-side norm of h; otherwise norm_x = norm1(h) (:340)
   float s3 = 0.f;
 #pragma unroll
   for (int v = 0; v < NV; ++v)
@@ -524,8 +555,13 @@ __global__ void __launch_bounds__(128, NV <= 3 ? 6 : 5) row_pre_resid_kernel(con
     if (lane + 32 * v < nch) {
       const int c = lane + 32 * v;
       float w1[8], h[8], b[8];
-      load8(reinterpret_cast<const T*>(p.norm1_w) + c * 8, w1);
       unpack8(uh[v], h);
+      if (p.mode == PRE_FINAL) {
+        chunk_norm<T>(h, s3, D, p.lhs_eps, reinterpret_cast<const T*>(p.lhs_w), reinterpret_cast<const T*>(p.lhs_b), c, b);
+        store8(reinterpret_cast<T*>(p.hf) + row + (size_t)c * 8, b);
+        continue;
+      }
+      load8(reinterpret_cast<const T*>(p.norm1_w) + c * 8, w1);
       chunk_norm_r<T>(h, s3, D, 1e-6f, w1, w1, false, b);
       store8(reinterpret_cast<T*>(p.norm_x) + row + (size_t)c * 8, b);
     }
