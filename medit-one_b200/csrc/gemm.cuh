@@ -587,13 +587,14 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
 // (tile = blockIdx.x + i * gridDim.x, the linear order above). Warp 0 streams A / B stages
 // through a kPStages-deep ring, warp 1 issues the MMAs into one of two TMEM accumulators
 // (columns [0, kPBN) and [kPBN, 2 kPBN)), and kPGroups groups of four epilogue warps (2..5,
-// 6..9, 10..13) drain the other accumulator, taking the kPChunk-token chunks in turn, each
-// group through its own staging tile, so a tile's epilogue runs under the next tile's main
-// loop. Same epilogue steps and rounding as tc_epilogue (no fused argmax).
+// 6..9, 10..13, 14..17) drain the other accumulator, taking the kPChunk-token chunks in turn
+// (four chunks a group per tile), each group through its own staging tile, so a tile's
+// epilogue runs under the next tile's main loop. Same epilogue steps and rounding as
+// tc_epilogue (no fused argmax).
 constexpr int kPStages = 4;
 constexpr int kPBN = 256;
 constexpr int kPChunk = 16;  // tokens per staging pass
-constexpr int kPGroups = 3;  // epilogue groups of four warps
+constexpr int kPGroups = 4;  // epilogue groups of four warps
 struct PCfg {
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = kPBN * 64 * 2;
