@@ -181,6 +181,7 @@ struct Launch {
     int n, r, E, k, group;
     unsigned long long tie;
     int np;  // > 0: moe_router_bf16_kernel<np> (input pairs per lane)
+    int staged;  // moe_router_bf16_kernel: rows copied ahead by cp.async
   } ro;
 };
 
@@ -465,7 +466,7 @@ static int run(const Launch& L, cudaStream_t st) {
 #define ONE_R2(NP)                                                                                                   \
   case NP:                                                                                                           \
     e = launch_k(moe_router_bf16_kernel<NP>, dim3(L.grid), dim3(L.block), L.smem, st, L.ro.R, L.ro.n, L.ro.r, L.ro.E, \
-                 L.ro.k, L.ro.group, L.ro.tie);                                                                      \
+                 L.ro.k, L.ro.group, L.ro.tie, L.ro.staged);                                                         \
     break;
           ONE_R2(1) ONE_R2(3) ONE_R2(6) ONE_R2(12) ONE_R2(24) ONE_R2(32)
 #undef ONE_R2
@@ -497,8 +498,13 @@ static int router_np(int in) {
 
 static int plan_router(Launch& L, const MoeRouter& R, int n, int r, int E, int k, int dtype) {
   auto a4 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 3) == 0; };
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   const int np = router_np(R.in);
-  const Router2Smem L2 = router2_smem(R.in, E);
+  // input rows and gate logits copied 16 bytes at a time: whole 16-byte rows, aligned. Only
+  // for wide inputs: the narrow instantiations run three CTAs per SM, which hide the row
+  // loads already (staging made the 144-input routers slower, 460 -> 497 us at 262,144 tokens)
+  const bool staged = np >= 12 && R.in % 8 == 0 && R.ldx % 8 == 0 && r % 8 == 0 && a16(R.x) && a16(R.glog);
+  const Router2Smem L2 = router2_smem(R.in, E, r, staged);
   if (dtype == ONE_DTYPE_BF16 && np > 0 && R.in % 2 == 0 && R.ldx % 2 == 0 && a4(R.x) && a4(R.comb) && a4(R.bias2) &&
       r <= 128 && E <= kMaxExperts && std::min(k, E) <= kR2MaxK && L2.warps >= 1) {
     const void* f = np == 1    ? (const void*)moe_router_bf16_kernel<1>
@@ -525,6 +531,7 @@ static int plan_router(Launch& L, const MoeRouter& R, int n, int r, int E, int k
     L.ro.group = group;
     L.ro.tie = topk_tie_selection(E, std::min(k, E));
     L.ro.np = np;
+    L.ro.staged = staged ? 1 : 0;
     return ONE_OK;
   }
   const int es = dtype == ONE_DTYPE_F32 ? 4 : 2;
