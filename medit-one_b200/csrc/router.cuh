@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf1
         const double tot = warp_transpose_sum8(a);
         if ((lane & 3) == 0 && e0 + slot < E) sc[u * E + e0 + slot] = __bfloat162float(__float2bfloat16_rn(__double2float_rn(tot)));
       }
-      __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
+      if (staged) __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
     }
     if (staged) cp_async_wait<0>();
     __syncwarp();
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf1
           out[pi] = pow2k ? pack_bf16x2(s0 * invk, s1 * invk) : pack_bf16x2(s0 / (float)kk, s1 / (float)kk);
         }
       }
-      __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
+      if (staged) __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
     }
     if (staged) cp_async_wait<0>();
     __syncwarp();

@@ -678,39 +678,42 @@ __global__ void __launch_bounds__(256) scan_mean_kernel(const ScanParams p) {
 }
 
 // Prefix mean of bf16 prompts with the (divisor, reciprocal) table, staged through shared
-// memory: a CTA owns one sequence and 128 features (64 threads, one feature pair each) and
-// keeps kScanStages - 1 tiles of kScanTok tokens x 256 bytes in flight with cp.async, so the
-// sequential fp32 sums read from shared memory while HBM streams the next tiles. Same
-// arithmetic, in the same order, as scan_mean_kernel's bf16 path.
+// memory: a CTA owns one sequence and 64 features (64 threads, one feature each: the sums
+// are sequential in the token, so B x D chains are all the parallelism there is) and keeps
+// kScanStages - 1 tiles of kScanTok tokens x 128 bytes in flight with cp.async, so the fp32
+// sums read from shared memory while HBM streams the next tiles. Same arithmetic, in the
+// same order, as scan_mean_kernel's bf16 path.
 constexpr int kScanTok = 64;
 constexpr int kScanStages = 4;
 constexpr int kScanThreads = 64;
-constexpr int kScanFeat = 2 * kScanThreads;
-constexpr size_t kScanSmem = (size_t)kScanStages * kScanTok * (kScanThreads * 4 + 8);
+constexpr int kScanFeat = kScanThreads;
+constexpr size_t kScanSmem = (size_t)kScanStages * kScanTok * (kScanFeat * 2 + 8);
 
 __global__ void __launch_bounds__(kScanThreads) scan_mean_staged_kernel(const ScanParams p) {
+  using T = __nv_bfloat16;
   extern __shared__ __align__(16) uint32_t ssm[];
   pdl_launch_dependents();
   const int groups = p.D / kScanFeat;
   const int bb = blockIdx.x / groups, g = blockIdx.x % groups, tid = threadIdx.x;
-  const int d = g * kScanFeat + 2 * tid;
-  uint32_t* xs = ssm;                                                                  // [stage][token][pair]
-  float2* ds = reinterpret_cast<float2*>(ssm + (size_t)kScanStages * kScanTok * kScanThreads);  // [stage][token]
+  const int d = g * kScanFeat + tid;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(ssm);  // [stage][token][feature]
+  float2* ds = reinterpret_cast<float2*>(ssm + (size_t)kScanStages * kScanTok * kScanFeat / 2);  // [stage][token]
   const size_t row = (size_t)p.D * 2;
   const uint8_t* xg = reinterpret_cast<const uint8_t*>(p.norm_x) + ((size_t)bb * p.S * p.D + g * kScanFeat) * 2;
-  uint32_t* mg = reinterpret_cast<uint32_t*>(p.mean) + ((size_t)bb * p.S * p.D + d) / 2;
+  uint16_t* mg = reinterpret_cast<uint16_t*>(p.mean) + (size_t)bb * p.S * p.D + d;
   const int nst = (p.S + kScanTok - 1) / kScanTok;
+  constexpr int kChunks = kScanFeat * 2 / 16;  // 16-byte chunks of a token's slice
   pdl_wait();
-  float a0 = p.state[(size_t)bb * p.D + d], a1 = p.state[(size_t)bb * p.D + d + 1];
-  // tile st: kScanTok rows of 16 chunks of 16 bytes, and its kScanTok table entries; an empty
-  // group past the end keeps the group count uniform
+  float a0 = p.state[(size_t)bb * p.D + d];
+  // tile st: kScanTok rows of kChunks chunks, and its kScanTok table entries; an empty group
+  // past the end keeps the group count uniform
   auto issue = [&](int st) {
     if (st < nst) {
       const int s0 = st * kScanTok, n = min(kScanTok, p.S - s0);
-      uint32_t* dst = xs + (size_t)(st % kScanStages) * kScanTok * kScanThreads;
-      for (int c = tid; c < n * 16; c += kScanThreads) {
-        const int t = c >> 4, q = c & 15;
-        cp_async16(dst + t * kScanThreads + q * 4, xg + (size_t)(s0 + t) * row + q * 16);
+      uint16_t* dst = xs + (size_t)(st % kScanStages) * kScanTok * kScanFeat;
+      for (int c = tid; c < n * kChunks; c += kScanThreads) {
+        const int t = c / kChunks, q = c % kChunks;
+        cp_async16(dst + t * kScanFeat + q * 8, xg + (size_t)(s0 + t) * row + q * 16);
       }
       if (tid < n) cp_async8(ds + (st % kScanStages) * kScanTok + tid, p.dr + s0 + tid);
     }
@@ -722,35 +725,28 @@ __global__ void __launch_bounds__(kScanThreads) scan_mean_staged_kernel(const Sc
     issue(st + kScanStages - 1);
     cp_async_wait<kScanStages - 1>();  // tile st has landed (this thread's copies)
     __syncthreads();                   // ... and every other thread's
-    const uint32_t* xv = xs + (size_t)(st % kScanStages) * kScanTok * kScanThreads + tid;
+    const uint16_t* xv = xs + (size_t)(st % kScanStages) * kScanTok * kScanFeat + tid;
     const float2* dv = ds + (st % kScanStages) * kScanTok;
     const int s0 = st * kScanTok, n = min(kScanTok, p.S - s0);
-    uint32_t* mo = mg + (size_t)s0 * (p.D / 2);
+    uint16_t* mo = mg + (size_t)s0 * p.D;
     if (n == kScanTok) {
 #pragma unroll 16
       for (int j = 0; j < kScanTok; ++j) {
-        const uint32_t v = xv[j * kScanThreads];
         const float2 q = dv[j];
-        a0 += bf2_lo(v);
-        a1 += bf2_hi(v);
-        mo[(size_t)j * (p.D / 2)] = pack_bf16x2(div_rn_recip(rnd<__nv_bfloat16>(a0), q.x, q.y),
-                                                div_rn_recip(rnd<__nv_bfloat16>(a1), q.x, q.y));
+        a0 += __uint_as_float((uint32_t)xv[j * kScanFeat] << 16);
+        mo[(size_t)j * p.D] = (uint16_t)(pack_bf16x2(div_rn_recip(rnd<T>(a0), q.x, q.y), 0.f) & 0xffffu);
       }
     } else {
       for (int j = 0; j < n; ++j) {
-        const uint32_t v = xv[j * kScanThreads];
         const float2 q = dv[j];
-        a0 += bf2_lo(v);
-        a1 += bf2_hi(v);
-        mo[(size_t)j * (p.D / 2)] = pack_bf16x2(div_rn_recip(rnd<__nv_bfloat16>(a0), q.x, q.y),
-                                                div_rn_recip(rnd<__nv_bfloat16>(a1), q.x, q.y));
+        a0 += __uint_as_float((uint32_t)xv[j * kScanFeat] << 16);
+        mo[(size_t)j * p.D] = (uint16_t)(pack_bf16x2(div_rn_recip(rnd<T>(a0), q.x, q.y), 0.f) & 0xffffu);
       }
     }
     __syncthreads();  // the tile's buffer is refilled by the next iteration's issue
   }
   cp_async_wait<0>();
   p.state[(size_t)bb * p.D + d] = a0;
-  p.state[(size_t)bb * p.D + d + 1] = a1;
 }
 
 // ------------------------------------------------------------------ final norm
