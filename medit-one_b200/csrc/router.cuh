@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf1
                                                                       int group, unsigned long long tie, int staged) {
   extern __shared__ __align__(16) uint8_t rsm[];
   const int in = R.in, hp = in / 2, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
-  const Router2Smem L = router2_smem(in, E, r, staged != 0);
+  const bool stg = NP >= 12 && staged != 0;  // the narrow instantiations carry no staging code
+  const Router2Smem L = router2_smem(in, E, r, stg);
   float* exs = reinterpret_cast<float*>(rsm + L.ex);
   uint8_t* wb = rsm + L.warp0 + warp * L.per_warp;
   float* cf = reinterpret_cast<float*>(wb + L.cf);  // [32][E] expert factors of the group
@@ -108,12 +109,12 @@ __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf1
   group = max(1, min(32, group));
   for (int t0 = (blockIdx.x * nwarp + warp) * group; t0 < ntok; t0 += gridDim.x * nwarp * group) {
     const int nt = min(group, ntok - t0);
-    if (staged) stage(t0, 0, nt, true);
+    if (stg) stage(t0, 0, nt, true);
     for (int u = 0; u < nt; ++u) {
       const int t = t0 + u;
       uint32_t xv[NP];
       const __nv_bfloat16* G = reinterpret_cast<const __nv_bfloat16*>(R.glog) + (size_t)t * r;
-      if (staged) {
+      if (stg) {
         stage(t0, u + 1, nt, true);
         cp_async_wait<1>();  // token u's copies (this lane's) have landed ...
         __syncwarp();        // ... and every lane's
@@ -186,9 +187,9 @@ __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf1
         const double tot = warp_transpose_sum8(a);
         if ((lane & 3) == 0 && e0 + slot < E) sc[u * E + e0 + slot] = __bfloat162float(__float2bfloat16_rn(__double2float_rn(tot)));
       }
-      if (staged) __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
+      if (stg) __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
     }
-    if (staged) cp_async_wait<0>();
+    if (stg) cp_async_wait<0>();
     __syncwarp();
     if (lane < nt) {  // top-k (:83-84), one token per lane
       topk_select_fast(sc + lane * E, E, kk, sel + lane * E, tie);
@@ -196,11 +197,11 @@ __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf1
         for (int j = 0; j < kk; ++j) R.idx_out[(size_t)(t0 + lane) * kk + j] = sel[lane * E + j];
     }
     __syncwarp();
-    if (staged) stage(t0, 0, nt, false);
+    if (stg) stage(t0, 0, nt, false);
     for (int u = 0; u < nt; ++u) {  // mean of the chosen biased inputs (:87-90)
       const int t = t0 + u;
       uint32_t xv[NP];
-      if (staged) {
+      if (stg) {
         stage(t0, u + 1, nt, false);
         cp_async_wait<1>();
         __syncwarp();
@@ -231,9 +232,9 @@ __global__ void __launch_bounds__(kR2Warps * 32, NP <= 6 ? 3 : 2) moe_router_bf1
           out[pi] = pow2k ? pack_bf16x2(s0 * invk, s1 * invk) : pack_bf16x2(s0 / (float)kk, s1 / (float)kk);
         }
       }
-      if (staged) __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
+      if (stg) __syncwarp();  // ring slot u & 1 is refilled by the next token's stage
     }
-    if (staged) cp_async_wait<0>();
+    if (stg) cp_async_wait<0>();
     __syncwarp();
   }
 }
