@@ -59,8 +59,9 @@ __global__ void prompt_table_kernel(const PromptTabParams p) {
 }
 
 // Shared memory (bytes): lin_q / lin_k / lin_v as [3][16][RS] bf16 (rows >= H zero), biases
-// [3][16] fp32, then per warp the token's q | k | v rows [3H][RS] bf16 and the output row
-// [H*H] bf16. RS = Dh + 16: a row stride of 8 (mod 32) words makes the warp's 8-byte
+// [3][16] fp32, then per warp two buffers of a token's q | k | v rows [3H][RS] bf16 (the next
+// token's rows are copied in by cp.async while the current token computes) and the output
+// row [H*H] bf16. RS = Dh + 16: a row stride of 8 (mod 32) words makes the warp's 8-byte
 // fragment loads (8 rows x 4 column groups) conflict-free.
 template <int DH>
 struct AttnTokSmem {
@@ -68,7 +69,8 @@ struct AttnTokSmem {
   static constexpr int W = 0;
   static constexpr int BIAS = 3 * 16 * RS * 2;
   static constexpr int WARP0 = BIAS + 3 * 16 * 4;
-  __host__ __device__ static int per_warp(int H) { return (3 * H * RS * 2 + H * H * 2 + 15) & ~15; }
+  __host__ __device__ static int rows_bytes(int H) { return 3 * H * RS * 2; }
+  __host__ __device__ static int per_warp(int H) { return (2 * rows_bytes(H) + H * H * 2 + 15) & ~15; }
   __host__ __device__ static int total(int H) { return WARP0 + kTokWarps * per_warp(H); }
 };
 
@@ -260,10 +262,25 @@ __global__ void __launch_bounds__(kTokWarps * 32, 2) attn_tok_kernel(const AttnT
   pdl_wait();
 
   uint8_t* wb = smb + S::WARP0 + warp * S::per_warp(H);
-  __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(wb);
-  uint32_t* stage = reinterpret_cast<uint32_t*>(wb + 3 * H * RS * 2);
-  for (int t = blockIdx.x * kTokWarps + warp; t < p.T; t += gridDim.x * kTokWarps) {
-    load_token_rows<DH>(p.proj + (size_t)t * 3 * HD, H, rows);
+  uint32_t* stage = reinterpret_cast<uint32_t*>(wb + 2 * S::rows_bytes(H));
+  // token t's q | k | v row into buffer b, 16-byte chunks; one commit group per call
+  auto issue = [&](int t, int b) {
+    if (t < p.T) {
+      constexpr int NCH = DH / 8;
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(p.proj + (size_t)t * 3 * HD);
+      uint8_t* dst = wb + b * S::rows_bytes(H);
+      for (int j = lane; j < 3 * H * NCH; j += 32) cp_async16(dst + ((j / NCH) * RS + (j % NCH) * 8) * 2, src + j * 16);
+    }
+    cp_async_commit();
+  };
+  const int stride = gridDim.x * kTokWarps;
+  int it = 0;
+  issue(blockIdx.x * kTokWarps + warp, 0);
+  for (int t = blockIdx.x * kTokWarps + warp; t < p.T; t += stride, ++it) {
+    issue(t + stride, (it + 1) & 1);
+    cp_async_wait<1>();  // this lane's copies of token t have landed ...
+    __syncwarp();        // ... and every lane's
+    const __nv_bfloat16* rows = reinterpret_cast<const __nv_bfloat16*>(wb + (it & 1) * S::rows_bytes(H));
     const __nv_bfloat16* tab = p.rope + (size_t)(t % p.seq_len) * DH;
     uint2 cs[DH / 32], sn[DH / 32];
 #pragma unroll
@@ -276,8 +293,9 @@ __global__ void __launch_bounds__(kTokWarps * 32, 2) attn_tok_kernel(const AttnT
     __syncwarp();
     uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (size_t)t * HH);
     for (int w = lane; w < HH / 2; w += 32) dst[w] = stage[w];
-    __syncwarp();
+    __syncwarp();  // buffer it & 1 is refilled by the next iteration's issue
   }
+  cp_async_wait<0>();
 }
 
 }  // namespace one
