@@ -88,8 +88,10 @@ class ClockSampler:
     def __init__(self, idx: int):
         self.idx = idx
         self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_rank{idx}.csv") if os.path.isdir(
-            os.path.join(REPO, "gpurun_out")) else f"/tmp/one_clocks_{os.getpid()}.csv"
+        # raw samples: kept in $ONE_CLOCKS_DIR when it is set (the JSON line carries the summary)
+        d = os.environ.get("ONE_CLOCKS_DIR")
+        self.path = os.path.join(d, f"clocks_rank{idx}.csv") if d and os.path.isdir(d) else \
+            f"/tmp/one_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
