@@ -149,7 +149,8 @@ int one_linear_moe(const void* x, int32_t n, int32_t fin, int32_t fout, const vo
  * library image of ONE_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library
  * until the process exits; calls needing more (n * fin too large) fail with ONE_ERR_INVALID.
  * The first call on a device looks the array's device address up (cudaGetSymbolAddress) with
- * that device current, so make that first call before any stream capture. Every call shares the
+ * that device current, so make that first call before any stream capture; a call made after a
+ * cudaDeviceReset (a new context) looks it up again. Every call shares the
  * one array: calls whose work overlaps on the GPU (other streams, other host threads) race;
  * serialise them. No call allocates or frees device memory. */
 #define ONE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
@@ -208,9 +209,10 @@ int one_ops_error(int32_t* where, int32_t clear);
 
 /* Self-test of the prompt path's prefix-mean division (a reciprocal table and one residual
  * correction instead of a division per element): every bf16 dividend (all 65536 bit
- * patterns) against each of the n divisors, compared with the fp32 division. mismatches[0]
- * counts fp32 results that differ, mismatches[1] results that differ after rounding to
- * bf16 (NaN equals NaN). Synchronises the device. (No reference counterpart.) */
+ * patterns) against each of the n divisors, compared with the fp32 division. mismatches is
+ * a caller-owned DEVICE array of two counters, zeroed by the call: [0] counts fp32 results
+ * that differ, [1] results that differ after rounding to bf16 (NaN equals NaN).
+ * Synchronises the stream. (No reference counterpart.) */
 int one_selftest_mean_division(const float* divisors, int32_t n, unsigned long long* mismatches, void* stream);
 
 #ifdef __cplusplus

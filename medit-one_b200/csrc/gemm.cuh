@@ -138,121 +138,6 @@ ONE_DEVINL void epi_gelu_pair(const GemmProblem& P, int n_even, int t, float g, 
 }
 
 
-// Whole-tile epilogue over a staged fp32 tile (kept for reference use by other kernels): S holds the
-// fp32 accumulator of rows n_base .. n_base+127 for tokens t_base .. t_base+tn-1, laid
-// out S[t_local * 128 + n_local]. Rows >= Nw are padding. Requires Nw % 8 == 0 (16 for
-// GELU_UP), 8-aligned leading dimensions and 16-byte-aligned pointers (checked by the
-// planner).
-template <typename T>
-__device__ __forceinline__ void epilogue_tile(const GemmProblem& P, const float* S, int n_base, int t_base, int tn,
-                                              int split, int nthreads) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
-  if (tn <= 0) return;
-  if (P.kind == EPI_ARGMAX) {
-    T* out = reinterpret_cast<T*>(P.out);
-    for (int tl = warp; tl < tn; tl += nwarps) {
-      const int nl = lane * 4;
-      const float4 f = *reinterpret_cast<const float4*>(S + tl * 128 + nl);
-      const float v[4] = {f.x, f.y, f.z, f.w};
-      unsigned long long key = 0ull;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int n = n_base + nl + e;
-        if (n < P.Nw) {
-          const unsigned long long k2 = argmax_key<T>(v[e], n);
-          key = k2 > key ? k2 : key;
-          if (out) st<T>(out + (size_t)(t_base + tl) * P.ldo + n, v[e]);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-        key = k2 > key ? k2 : key;
-      }
-      if (lane == 0 && key) atomicMax(P.best + t_base + tl, key);
-    }
-    return;
-  }
-  if (P.kind == EPI_GELU_UP) {
-    // 128 interleaved rows -> 64 output features; unit = (token, 8 outputs)
-    T* out = reinterpret_cast<T*>(P.out);
-    for (int u = tid; u < tn * 8; u += nthreads) {
-      const int tl = u >> 3, c = u & 7;
-      const int n0 = n_base + c * 16;
-      if (n0 >= P.Nw) continue;
-      const float* sv = S + tl * 128 + c * 16;
-      float g[16];
-#pragma unroll
-      for (int i = 0; i < 16; i += 4) {
-        const float4 f = *reinterpret_cast<const float4*>(sv + i);
-        g[i] = f.x; g[i + 1] = f.y; g[i + 2] = f.z; g[i + 3] = f.w;
-      }
-      float b[16];
-      if (P.bias) {
-        load8(reinterpret_cast<const T*>(P.bias) + n0, b);
-        load8(reinterpret_cast<const T*>(P.bias) + n0 + 8, b + 8);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) b[i] = 0.f;
-      }
-      float o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float gb = rnd<T>(g[2 * j] + b[2 * j]);
-        const float ub = rnd<T>(g[2 * j + 1] + b[2 * j + 1]);
-        o[j] = rnd<T>(gelu_erf(gb)) * ub;
-      }
-      store8(out + (size_t)(t_base + tl) * P.ldo + (n0 >> 1), o);
-    }
-    return;
-  }
-  // STORE / HXPRE / XMOE / CX / PARTIAL: unit = (token, 8 rows)
-  for (int u = tid; u < tn * 16; u += nthreads) {
-    const int tl = u >> 4, c = u & 15;
-    const int n0 = n_base + c * 8;
-    if (n0 >= P.Nw) continue;
-    const int t = t_base + tl;
-    float a[8];
-    {
-      const float4 f0 = *reinterpret_cast<const float4*>(S + tl * 128 + c * 8);
-      const float4 f1 = *reinterpret_cast<const float4*>(S + tl * 128 + c * 8 + 4);
-      a[0] = f0.x; a[1] = f0.y; a[2] = f0.z; a[3] = f0.w; a[4] = f1.x; a[5] = f1.y; a[6] = f1.z; a[7] = f1.w;
-    }
-    if (P.kind == EPI_PARTIAL) {
-      store8(P.ws + ((size_t)split * P.T + t) * P.ldw + n0, a);
-      continue;
-    }
-    if (P.bias) {
-      float b[8];
-      load8(reinterpret_cast<const T*>(P.bias) + n0, b);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) a[e] += b[e];
-    }
-    T* out = reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n0;
-    if (P.kind == EPI_STORE) {
-      store8(out, a);
-    } else if (P.kind == EPI_CX) {
-      float y[8], z[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        y[e] = rnd<T>(a[e]);
-        z[e] = fminf(fmaxf(y[e], -1e4f), 1e4f);
-      }
-      store8(out, y);
-      store8(reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0, z);
-    } else {  // HXPRE: aux + clamp(y); XMOE: aux * clamp(y)
-      float x[8], y[8];
-      load8(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0, x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float cl = fminf(fmaxf(rnd<T>(a[e]), -100.f), 100.f);
-        y[e] = P.kind == EPI_HXPRE ? x[e] + cl : x[e] * cl;
-      }
-      store8(out, y);
-    }
-  }
-}
-
 // ------------------------------------------------------------------ tensor-core kernel
 template <int BN>
 struct TcCfg {

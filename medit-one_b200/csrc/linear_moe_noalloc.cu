@@ -10,6 +10,7 @@
 // is part of the library image: every GPU that loads the library holds
 // ONE_NOALLOC_SCRATCH_BYTES of device memory for it until the process exits, and no call
 // allocates or frees anything.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -26,18 +27,52 @@ namespace {
 __device__ __align__(256) unsigned char g_noalloc_scratch[ONE_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchSlot {
+  void* addr;
+  unsigned long long ctx_id;  // the CUDA context the address belongs to (0 = unknown)
+};
+ScratchSlot g_scratch[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 
-// Device address of the scratch on the current device; looked up once per device, with that
-// device current, on the first call made there.
+// Unique id of the calling thread's current CUDA context (cuCtxGetId, never reused within the
+// process), or 0 when it cannot be read. A cudaDeviceReset destroys the context that the cached
+// address belongs to; the next context has a new id, so the address is looked up again.
+unsigned long long current_context_id() {
+  typedef CUresult (*GetCurrentFn)(CUcontext*);
+  typedef CUresult (*GetIdFn)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of the scratch on the current device. Looked up (cudaGetSymbolAddress) with
+// that device current on the first call made there, and again whenever the device's context
+// changed since (after a cudaDeviceReset); otherwise the cached address is returned.
 int scratch_on_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return one_set_error(ONE_ERR_CUDA, cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return one_set_error(ONE_ERR_UNSUPPORTED, "device index out of range");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  ScratchSlot& slot = g_scratch[dev];
+  const unsigned long long ctx = slot.addr ? current_context_id() : 0;
+  if (!slot.addr || ctx == 0 || ctx != slot.ctx_id) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) {
@@ -45,9 +80,10 @@ int scratch_on_current_device(void** out) {
       snprintf(msg, sizeof(msg), "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
       return one_set_error(ONE_ERR_CUDA, msg);
     }
-    g_scratch_addr[dev] = p;
+    slot.addr = p;
+    slot.ctx_id = current_context_id();  // the lookup made the device's context current
   }
-  *out = g_scratch_addr[dev];
+  *out = slot.addr;
   return ONE_OK;
 }
 

@@ -47,14 +47,13 @@ def decode_divisors(max_pos: int, dtype: torch.dtype) -> torch.Tensor:
         out[0] = 1.0
         out[1:] = torch.arange(1, max_pos + 1, dtype=torch.float32)
         return out
-    exact = torch.arange(0, max_pos + 1, dtype=torch.float32).to(dtype).float()
-    out.copy_(exact)
+    # Every entry comes from arange itself: which positions differ from dtype(P) depends on
+    # the host CPU's vector width and on where arange's scalar tail starts (on one AVX-512
+    # host, P = 32897, 33153, ... (129 mod 256) give dtype(P) - 256), so no position is
+    # inferred. ~50 us per entry.
     out[0] = arange_last(1, dtype)
     for p in range(1, max_pos + 1):
-        # positions in arange's scalar tail round exactly; the vectorised body only
-        # covers multiples of the (>= 16-lane pair) vector width
-        if p <= 4096 or p % 16 == 0:
-            out[p] = arange_last(p, dtype)
+        out[p] = arange_last(p, dtype)
     return out
 
 
@@ -63,10 +62,26 @@ def prompt_divisors(seq_len: int, dtype: torch.dtype) -> torch.Tensor:
     return (torch.arange(1, seq_len + 1, dtype=dtype) + 1e-10).float()
 
 
+def check_supported(config) -> None:
+    """Raise NotImplementedError for OneConfig switches whose reference behaviour the engine
+    does not compute, instead of silently running the default path.
+
+    * ``use_flash_attention=True`` replaces the feature-level softmax with causal attention
+      across the call's tokens (one/modeling_one.py:408-421, TurboFlashAttention in
+      one/turbo_ops.py:437-475).
+    * ``use_single_token=True`` computes the attention of each sequence's last position only
+      and broadcasts it over the sequence (one/modeling_one.py:338, 550-568).
+    """
+    for flag in ("use_flash_attention", "use_single_token"):
+        if getattr(config, flag, False):
+            raise NotImplementedError(f"OneConfig.{flag}=True is not supported by the B200 engine")
+
+
 class OneEngine:
     def __init__(self, config, state_dict: Dict[str, torch.Tensor], device="cuda", dtype=torch.bfloat16,
                  max_batch: int = 256, max_tokens: Optional[int] = None, hist_cap: int = 4096,
                  max_positions: int = 8192):
+        check_supported(config)
         if not torch.cuda.is_available():
             raise C.OneError("OneEngine needs a CUDA device (B200, sm_100a)")
         self.cfg = config

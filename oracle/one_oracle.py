@@ -486,13 +486,14 @@ class ForwardResult:
 
 
 def forward(sd: Dict[str, Tensor], ids: Tensor, cfg: OracleConfig, dtype: torch.dtype,
-            history: Optional[List[Tensor]] = None) -> ForwardResult:
+            history: Optional[List[Tensor]] = None, last_only: bool = False) -> ForwardResult:
     """OneForCausalLM.forward (one/modeling_one.py:671-826, 857-926) over ``ids [b, s]``.
 
     ``history`` is the per-layer DynamicCache content (norm_x of earlier tokens,
     [b, P, D] each) or None for a cache-free forward. It is extended in place,
     exactly as ``past_key_value.update`` does (:358-365).
-    Returns the logits, the last layer's (hx, cx) and the per-layer norm_x.
+    Returns the logits (of the last position only when ``last_only``; the other outputs are
+    unchanged), the last layer's (hx, cx) and the per-layer norm_x.
     """
     b, s = ids.shape
     P = 0 if history is None or len(history) == 0 else history[0].shape[1]
@@ -523,7 +524,7 @@ def forward(sd: Dict[str, Tensor], ids: Tensor, cfg: OracleConfig, dtype: torch.
         out, hx, cx, norm_x = one_layer(h, hx, cx, lp, cos, sin, mean_fn, cfg)
         norms.append(norm_x)
         h = h + out                                                                    # :793
-    return ForwardResult(_final(sd, h, cfg), hx, cx, norms)
+    return ForwardResult(_final(sd, h[:, -1:] if last_only else h, cfg), hx, cx, norms)
 
 
 class RunningDecoder:
@@ -544,8 +545,8 @@ class RunningDecoder:
         self.inv_freq = rope_inv_freq(cfg.head_dim, cfg.rope_theta)
         self.layers = [layer_params(sd, i, cfg) for i in range(cfg.num_hidden_layers)]
 
-    def prefill(self, ids: Tensor) -> ForwardResult:
-        res = forward(self.sd, ids, self.cfg, self.dtype, history=None)
+    def prefill(self, ids: Tensor, last_only: bool = False) -> ForwardResult:
+        res = forward(self.sd, ids, self.cfg, self.dtype, history=None, last_only=last_only)
         self.S = []
         for nx in res.norm_x:
             acc = torch.zeros(nx.shape[0], nx.shape[2], dtype=torch.float32)

@@ -1,7 +1,8 @@
 """Generate the golden fixtures in this directory by running the MedIT One
 reference itself (its PyTorch CPU path) on seeded inputs.
 
-Usage:  python tests/golden/make_golden.py [/path/to/reference]
+Usage:  python tests/golden/make_golden.py /path/to/reference
+        (or set ONE_REFERENCE_DIR to the reference source tree)
 
 The reference targets transformers 4.x; on the installed transformers 5.5 it
 needs three patches, applied here before any model is built and without editing
@@ -28,7 +29,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ONE_REFERENCE_DIR")
+if not REF or not os.path.isdir(os.path.join(REF, "one")):
+    sys.exit("usage: make_golden.py /path/to/reference (the MedIT One source tree, holding one/)")
 
 
 def _load(name, path):

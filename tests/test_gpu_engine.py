@@ -53,7 +53,16 @@ def test_forward_logits_and_state_match_reference(dt):
     assert eng.device_error() == (0, 0)
     lg = lg.float().cpu()
     assert_close(lg[..., :512].numpy(), g["logits_slice"], dt, "logits")
-    assert (lg.argmax(-1).numpy() == g["logits_argmax"]).mean() > 0.95
+    # every position's argmax is the reference's, or a near-tie of the oracle's full logits
+    from oracle import one_oracle as O
+    from parity_util import near_tie_ok
+    from test_oracle_golden import ocfg
+    am = lg.argmax(-1).view(-1)
+    ref = O.forward(sd, torch.from_numpy(g["ids"]), ocfg(cfg), DT[dt]).logits.view(-1, cfg.vocab_size)
+    ok, excused = near_tie_ok(ref, am)
+    assert bool(ok.all()), f"{int((~ok).sum())} positions pick a token that is not a near-tie of the oracle's argmax"
+    same = am.numpy() == g["logits_argmax"].reshape(-1)
+    assert bool((same | excused.numpy()).all())
     hx, cx = eng.last_hx_cx(128)
     assert_close(hx.float().cpu().view(2, 64, -1).numpy(), g["hx"], dt, "hx")
     assert_close(cx.float().cpu().view(2, 64, -1).numpy(), g["cx"], dt, "cx")
@@ -78,17 +87,25 @@ def test_cached_decode_matches_reference(dt):
 
 
 def test_greedy_decode_matches_reference_bf16():
-    """Autonomous greedy decode (argmax fed back on the device) reproduces the tokens."""
+    """Autonomous greedy decode (argmax fed back on the device): every token is the oracle's
+    argmax given the engine's own prefix, or a near-tie of it (parity_util); with no near-tie
+    the tokens equal the reference's exactly."""
+    from oracle import one_oracle as O
+    from parity_util import check_greedy_tokens
+    from test_oracle_golden import ocfg
     g = load("decode_bf16.npz")
     cfg, sd = tiny_sd("bf16")
     eng = make_engine(cfg, sd, "bf16", max_batch=3, max_tokens=64)
-    eng.prefill(torch.from_numpy(g["prompt"]).cuda())
+    prompt = torch.from_numpy(g["prompt"])
+    eng.prefill(prompt.cuda())
     steps = g["generated"].shape[1]
     for _ in range(steps):
         eng.step(None, next_ids=False)
     torch.cuda.synchronize()
-    got = eng.history(steps, 3).cpu().numpy().T
-    assert (got == g["generated"]).mean() >= 0.9, (got, g["generated"])
+    got = eng.history(steps, 3).cpu().T.contiguous()
+    excused = check_greedy_tokens(O.RunningDecoder(sd, ocfg(cfg), torch.bfloat16), prompt, got, what="greedy")
+    if excused == 0:
+        assert (got.numpy() == g["generated"]).all(), (got, g["generated"])
     assert eng.counters() == (12 + steps, steps)
 
 

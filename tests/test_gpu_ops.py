@@ -104,12 +104,12 @@ def test_prefix_mean_division_is_exact():
     from one import _capi as C
     from one.engine import prompt_divisors
     div = torch.unique(prompt_divisors(16384, torch.bfloat16)).cuda()
-    mism = (ctypes.c_ulonglong * 2)()
-    C.check(C.LIB.one_selftest_mean_division(C.ptr(div), div.numel(), ctypes.addressof(mism),
+    mism = torch.full((2,), -1, dtype=torch.int64, device="cuda")
+    C.check(C.LIB.one_selftest_mean_division(C.ptr(div), div.numel(), C.ptr(mism),
                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
             "one_selftest_mean_division")
     assert div.numel() > 500
-    assert (mism[0], mism[1]) == (0, 0)
+    assert mism.cpu().tolist() == [0, 0]
 
 
 def test_linear_moe_all_ties_reference_order():
@@ -222,4 +222,12 @@ def test_causal_lm_api_matches_reference():
         out = model(input_ids=gen[:, s:s + 1], past_key_values=cache, use_cache=True)
         assert_close(out.logits[:, 0].float().cpu()[:, :512].numpy(), d["logits_slice"][s], "bf16", f"decode {s}")
     seq = model.generate_greedy(torch.from_numpy(d["prompt"]).cuda(), gen.shape[1])
-    assert (seq[:, 12:].cpu().numpy() == d["generated"]).mean() >= 0.9
+    # each generated token is the oracle's argmax given the same prefix, or a near-tie of it
+    from oracle import one_oracle as O
+    from parity_util import check_greedy_tokens
+    from test_oracle_golden import ocfg
+    sd16 = {k: v.to(torch.bfloat16) for k, v in sd.items()}
+    excused = check_greedy_tokens(O.RunningDecoder(sd16, ocfg(cfg), torch.bfloat16), torch.from_numpy(d["prompt"]),
+                                  seq[:, 12:].cpu(), what="generate_greedy")
+    if excused == 0:
+        assert (seq[:, 12:].cpu().numpy() == d["generated"]).all()

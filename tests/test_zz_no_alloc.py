@@ -22,7 +22,10 @@ def _params(fin, fout, E, r, seed, dt):
     return {k: v.cuda().contiguous() for k, v in moe_params(fin, fout, E, r, seed, dt).items()}
 
 
-def _call(fn_name, x, p, k, with_ws):
+def _call(fn_name, x, p, k, with_ws, free_bytes=None):
+    """One LinearMoE call through the C ABI. With free_bytes (a list), the device's free memory
+    (cudaMemGetInfo) is appended before and after the call itself, all buffers being allocated
+    before the first reading."""
     from one import _capi as C
     n, fin = x.shape
     fout, E, r = p["weight"].shape[0], p["experts"].numel(), p["gate"].shape[0]
@@ -37,7 +40,13 @@ def _call(fn_name, x, p, k, with_ws):
         ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
         C.check(C.LIB.one_linear_moe(*args, C.ptr(ws), wsb, stream), "one_linear_moe")
     else:
+        torch.cuda.synchronize()
+        if free_bytes is not None:
+            free_bytes.append(torch.cuda.mem_get_info()[0])
         C.check(getattr(C.LIB, fn_name)(*args, stream), fn_name)
+        torch.cuda.synchronize()
+        if free_bytes is not None:
+            free_bytes.append(torch.cuda.mem_get_info()[0])
     torch.cuda.synchronize()
     return out, idx
 
@@ -49,9 +58,13 @@ def test_noalloc_matches_workspace_entry_twice(dt):
         p = _params(fin, fout, 8, 64, seed, dt)
         x = torch.randn(n, fin, generator=torch.Generator().manual_seed(seed)).to(dt).cuda()
         ref, ref_idx = _call(None, x, p, 2, with_ws=True)
-        got, got_idx = _call("one_linear_moe_noalloc", x, p, 2, with_ws=False)
+        free = []
+        got, got_idx = _call("one_linear_moe_noalloc", x, p, 2, with_ws=False, free_bytes=free)
         np.testing.assert_array_equal(got_idx.cpu().numpy(), ref_idx.cpu().numpy(), err_msg=f"call {call}")
         np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), err_msg=f"call {call}", **tol)
+        # the entry point's contract: the call itself takes no device memory (the device's free
+        # bytes are unchanged across it; the scratch was reserved when the library loaded)
+        assert free[0] == free[1], f"call {call}: free device memory {free[0]} -> {free[1]}"
 
 
 def test_noalloc_rejects_oversized_request():
