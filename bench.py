@@ -218,17 +218,28 @@ def run_reference(args, ws, rank):
 
 
 def run_native(args, ws, rank, local):
+    from one import distributed as Dd
     from one.configuration_one import config_140m
     from one.engine import OneEngine
     from one.initialization import init_state_dict
     cfg = config_140m()
     sd = init_state_dict(cfg, SEED, torch.bfloat16)
     steps, warmup = args.steps, args.warmup
-    eng = OneEngine(cfg, sd, f"cuda:{local}", torch.bfloat16, max_batch=BATCH, max_tokens=BATCH * PROMPT,
-                    hist_cap=max(steps + warmup + 64, 256), max_positions=PROMPT + 2 * (steps + warmup) + 4096)
+    strong = args.global_batch is not None
+    if strong:
+        # fixed global batch, split by sequence: rank r decodes its contiguous shard of one
+        # seeded prompt set
+        G = args.global_batch
+        first, bl = Dd.shard(G, ws, rank)
+        g = torch.Generator().manual_seed(SEED)
+        prompt = torch.randint(0, cfg.vocab_size, (G, PROMPT), generator=g)[first:first + bl]
+    else:
+        G, bl = BATCH * ws, BATCH
+        g = torch.Generator().manual_seed(SEED + rank)
+        prompt = torch.randint(0, cfg.vocab_size, (BATCH, PROMPT), generator=g)
+    eng = OneEngine(cfg, sd, f"cuda:{local}", torch.bfloat16, max_batch=bl, max_tokens=bl * PROMPT,
+                    hist_cap=2 * (steps + warmup) + 64, max_positions=PROMPT + 2 * (steps + warmup) + 4096)
     del sd
-    g = torch.Generator().manual_seed(SEED + rank)
-    prompt = torch.randint(0, cfg.vocab_size, (BATCH, PROMPT), generator=g)
     eng.prefill(prompt.cuda())
     eng.capture(1)
     stream = torch.cuda.current_stream()
@@ -236,40 +247,52 @@ def run_native(args, ws, rank, local):
         eng.replay()
     torch.cuda.synchronize()
     barrier(ws)
+    # The timed region: the K graph-replayed steps, then the run's only collective, the NCCL
+    # all-gather of every rank's generated tokens of those steps to every rank.
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         start.record(stream)
         for _ in range(steps):
             eng.replay()
+        tokens = Dd.gather_tokens(eng.history(warmup + steps, bl)[warmup:].t().contiguous(), G)
         end.record(stream)
         end.synchronize()
     torch.cuda.synchronize()
     barrier(ws)
+    assert tokens.shape == (G, steps)
     ms = start.elapsed_time(end)
     ms_max = max_over_ranks(ws, ms)
     code = eng.device_error()
     if code != (0, 0):
         raise RuntimeError(f"device error {code}")
-    value = ws * BATCH * steps / (ms_max / 1000.0)
-    # outside the timed region: every rank's generated tokens to every rank (NCCL all-gather)
-    from one import distributed as Dd
-    tokens = Dd.gather_tokens(eng.history(min(steps + warmup, eng.hist_cap), BATCH).t().contiguous(), BATCH * ws)
-    assert tokens.shape[0] == BATCH * ws
+    value = G * steps / (ms_max / 1000.0)
+    # the gather alone, for the record (same collective, same sizes)
+    gather_ms = None
+    if ws > 1:
+        torch.cuda.synchronize()
+        barrier(ws)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        Dd.gather_tokens(eng.history(warmup + steps, bl)[warmup:].t().contiguous(), G)
+        g1.record(stream)
+        g1.synchronize()
+        gather_ms = max_over_ranks(ws, g0.elapsed_time(g1))
 
-    # e2e through the public step API: pinned host ids in, next ids out, every step
-    ids_host = torch.randint(0, cfg.vocab_size, (BATCH,), dtype=torch.int32, generator=g).pin_memory()
-    out_host = torch.empty(BATCH, dtype=torch.int32).pin_memory()
-    ids_dev = torch.empty(BATCH, dtype=torch.int32, device=f"cuda:{local}")
+    # e2e through the public step API: pinned host ids in, next ids out, every step; the
+    # run's tokens all-gathered at the end (inside the timed region)
+    ids_host = torch.randint(0, cfg.vocab_size, (bl,), dtype=torch.int32, generator=g).pin_memory()
+    out_host = torch.empty(bl, dtype=torch.int32).pin_memory()
+    ids_dev = torch.empty(bl, dtype=torch.int32, device=f"cuda:{local}")
     for _ in range(max(warmup, 2)):
         ids_dev.copy_(ids_host, non_blocking=True)
         _, nx = eng.step(ids_dev)
         out_host.copy_(nx, non_blocking=True)
         torch.cuda.current_stream().synchronize()
+    done = eng.counters()[1]
     barrier(ws)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
     e_start.record(stream)
     for _ in range(steps):
         ids_dev.copy_(ids_host, non_blocking=True)
@@ -277,34 +300,40 @@ def run_native(args, ws, rank, local):
         out_host.copy_(nx, non_blocking=True)
         stream.synchronize()
         ids_host.copy_(out_host)
+    e_tokens = Dd.gather_tokens(eng.history(done + steps, bl)[done:].t().contiguous(), G)
     e_end.record(stream)
     e_end.synchronize()
+    assert e_tokens.shape == (G, steps)
     e_ms = max_over_ranks(ws, e_start.elapsed_time(e_end))
-    e2e = ws * BATCH * steps / (e_ms / 1000.0)
+    e2e = G * steps / (e_ms / 1000.0)
 
     hbm, tf, tf_sus, src = peaks()
-    sb = step_bytes(cfg, BATCH)
+    sb = step_bytes(cfg, bl)
     t_step = ms_max / 1000.0 / steps
     achieved = sb["total"] / t_step / 1e9
-    launches = eng.step_launches(BATCH)
+    launches = eng.step_launches(bl)
     clocks = clk.summary()
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": steps, "warmup": warmup,
-            "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "metric": METRIC if not strong else f"decode tok/s (140M-class bf16, global batch {G})",
+            "value": value, "unit": "tok/s", "n_gpus": ws, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02) seed 4, uniform prompt ids)",
             "config": {"workload": "140M-class One (vocab 32000, hidden 768, 12 layers, 12 heads, 8 experts top-2, "
                                    "FFN 3072), bf16 greedy decode after a 128-token prompt",
-                       "batch_per_gpu": BATCH, "global_batch": BATCH * ws, "prompt": PROMPT,
-                       "parallelism": f"sequence-sharded dp{ws}, no collective on the step path",
+                       "batch_per_gpu": bl, "global_batch": G, "prompt": PROMPT,
+                       "parallelism": f"sequence-sharded dp{ws}, no collective on the step path; one NCCL "
+                                      f"all-gather of the generated tokens per timed run, inside the timed region",
+                       "gather_ms": gather_ms,
                        "l2": "inputs larger than L2 (285 MB of weights streamed per step)"},
             "roofline": {"bound": "hbm", "kernel": f"decode step ({launches} launches, CUDA graph)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_source": src, "traffic": None, "algorithmic_bytes_per_step": sb["total"],
                          "tflops_achieved": sb["flops"] / t_step / 1e12,
                          "tensor_frac_sustained": sb["flops"] / t_step / 1e12 / tf_sus},
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": BATCH * 4, "d2h_bytes_per_step": BATCH * 4},
-            "gpu_launches": launches * steps,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": bl * 4, "d2h_bytes_per_step": bl * 4},
+            "gpu_launches": launches * steps + (1 if ws > 1 else 0),
             "clocks": clocks,
         }
         if ws == 1 and not args.no_cpu_baseline:
@@ -755,6 +784,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="decode: fixed global batch split over the GPUs (strong scaling); default 256 per GPU")
     ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
     ap.add_argument("--profile-prefill", action="store_true", help="run the small prompt-ingestion ncu case and exit")
     ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe", "prefill"],

@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // the weight copy and the token copy of the slot arrive
       mbar_init(&empty[s], 1);
     }
     mbar_init(accb, 1);
@@ -418,23 +418,27 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
 
   if (warp == 0) {
     if (lane == 0) {
-      // Weights do not depend on the previous kernel: request the first stages before
-      // waiting on it, so the HBM stream overlaps the previous kernel's tail.
+      // Weights do not depend on the previous kernel: the first stages are requested before
+      // the dependency wait, so the HBM stream overlaps the previous kernel's tail.
       const uint64_t wpol = l2_policy_evict_first();
-      const int pre = min(nkb, C::kStages);
-      for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-        tma_load_2d_hint(sA(i), &p.tmw[pi], &full[i], (kb0 + i) * 64, m_tile * 128, wpol);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % C::kStages;
+        const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
+        if (i >= C::kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
+        mbar_arrive_expect_tx(&full[s], C::kABytes);
+        tma_load_2d_hint(sA(s), &p.tmw[pi], &full[s], (kb0 + i) * 64, m_tile * 128, wpol);
       }
+    }
+  } else if (warp == 5) {
+    // The token tiles come from another warp: one thread's bulk copies complete one after
+    // another (~0.46 us each on B200), so two issuing threads halve the stream's length.
+    if (lane == 0) {
       pdl_wait();
       for (int i = 0; i < nkb; ++i) {
         const int s = i % C::kStages;
         const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
-        if (i >= pre) {
-          if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
-          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-          tma_load_2d_hint(sA(s), &p.tmw[pi], &full[s], (kb0 + i) * 64, m_tile * 128, wpol);
-        }
+        if (i >= C::kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
+        mbar_arrive_expect_tx(&full[s], C::kBBytes);
         tma_load_2d(sB(s), &p.tmx[pi], &full[s], (kb0 + i) * 64, n_tile * BN);
       }
     }

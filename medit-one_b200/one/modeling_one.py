@@ -22,6 +22,12 @@ from .configuration_one import OneConfig
 from .linear_moe import LinearMoE
 
 
+try:  # transformers >= 5: init helpers that skip parameters loaded from a checkpoint
+    from transformers import initialization as _init
+except ImportError:  # transformers 4.x initialises only missing parameters itself
+    _init = nn.init
+
+
 class OneRMSNorm(nn.Module):
     """Parameters of one/modeling_one.py:55-70."""
 
@@ -96,14 +102,17 @@ class OnePreTrainedModel(PreTrainedModel):
     _no_split_modules = ["One"]
 
     def _init_weights(self, module):
+        # from_pretrained calls this after loading the checkpoint: the transformers init helpers
+        # leave parameters that the checkpoint provided (_is_hf_initialized) untouched
         if isinstance(module, nn.Linear) and not isinstance(module, LinearMoE):
-            module.weight.data.normal_(mean=0.0, std=0.01)
+            _init.normal_(module.weight, mean=0.0, std=0.01)
             if module.bias is not None:
-                module.bias.data.zero_()
+                _init.zeros_(module.bias)
         elif isinstance(module, nn.Embedding):
-            module.weight.data.normal_(mean=0.0, std=0.01)
-            if module.padding_idx is not None:
-                module.weight.data[module.padding_idx].zero_()
+            _init.normal_(module.weight, mean=0.0, std=0.01)
+            if module.padding_idx is not None and not getattr(module.weight, "_is_hf_initialized", False):
+                with torch.no_grad():
+                    module.weight[module.padding_idx].zero_()
 
 
 class OneEngineCache:
