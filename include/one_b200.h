@@ -215,6 +215,19 @@ int one_ops_error(int32_t* where, int32_t clear);
  * Synchronises the stream. (No reference counterpart.) */
 int one_selftest_mean_division(const float* divisors, int32_t n, unsigned long long* mismatches, void* stream);
 
+/* One token per sequence drawn from logits [batch][ld] (first `vocab` entries, model dtype),
+ * warped as transformers' generation loop warps fp32 logits for do_sample=True
+ * (generation/utils.py _get_logits_processor, sampling branch; transformers 5.5): scores / T,
+ * then top-k (keep scores >= the k-th largest; top_k = 0: off), then top-p (keep the largest
+ * tokens until their probability mass reaches top_p; top_p >= 1: off), then one draw from the
+ * softmax of the kept scores. Ties at a top-k / top-p boundary are all kept. The draw for
+ * sequence b uses the Philox4x32-10 counter (offset, b) under key `seed`, so equal (seed,
+ * offset) give equal tokens. vocab <= 49152; temperature > 0. out [batch] int32 (device).
+ * No counterpart in one_turbo: it replaces the sampling step of GenerationMixin.generate,
+ * which the reference's generate() runs (one/modeling_one.py:845, README.md:73). */
+int one_sample_tokens(const void* logits, int32_t batch, int32_t vocab, int32_t ld, int32_t dtype, float temperature,
+                      int32_t top_k, float top_p, uint64_t seed, uint64_t offset, int32_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -335,3 +335,22 @@ extern "C" int one_selftest_mean_division(const float* divisors, int32_t n, unsi
   if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "division self-test: %s", cudaGetErrorString(e));
   return ONE_OK;
 }
+
+extern "C" int one_sample_tokens(const void* logits, int32_t batch, int32_t vocab, int32_t ld, int32_t dtype,
+                                 float temperature, int32_t top_k, float top_p, uint64_t seed, uint64_t offset,
+                                 int32_t* out, void* stream) {
+  if (!logits || !out) return fail(ONE_ERR_INVALID, "null argument");
+  if (batch < 1 || vocab < 1 || ld < vocab) return fail(ONE_ERR_INVALID, "bad sizes");
+  if (vocab > kSampMaxVocab) return fail(ONE_ERR_UNSUPPORTED, "vocabulary of at most %d entries", kSampMaxVocab);
+  if (!(temperature > 0.0f)) return fail(ONE_ERR_INVALID, "temperature must be positive (do_sample=False is greedy)");
+  if (top_k < 0 || !(top_p > 0.0f)) return fail(ONE_ERR_INVALID, "top_k >= 0 and top_p > 0");
+  if (dtype != ONE_DTYPE_BF16 && dtype != ONE_DTYPE_F32) return fail(ONE_ERR_INVALID, "dtype");
+  int rc = set_kernel_attrs();
+  if (rc) return rc;
+  SampleParams p{logits, batch, vocab, ld, dtype, temperature, top_k, top_p, (unsigned long long)seed,
+                 (unsigned long long)offset, out};
+  const cudaError_t e = launch_k(sample_kernel, dim3(batch), dim3(kSampThreads), (size_t)vocab * 4,
+                                 (cudaStream_t)stream, p);
+  if (e != cudaSuccess) return fail(ONE_ERR_CUDA, "sample launch: %s", cudaGetErrorString(e));
+  return ONE_OK;
+}

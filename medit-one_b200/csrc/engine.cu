@@ -36,6 +36,7 @@
 #include "attn_tok.cuh"
 #include "router.cuh"
 #include "dec_attn.cuh"
+#include "sample.cuh"
 
 using namespace one;
 
@@ -118,7 +119,7 @@ struct ProbSpec {
 
 enum LaunchKind {
   L_GEMM_TC, L_GEMM_SIMT, L_ROW_PRE, L_ROW_ATTN, L_SCAN, L_ROW_NORM, L_ADVANCE, L_NEXT_IDS,
-  L_PROMPT_TAB, L_ATTN_TOK, L_ROUTER, L_ROW_PRE_W, L_DEC_ATTN
+  L_PROMPT_TAB, L_ATTN_TOK, L_ROUTER, L_ROW_PRE_W, L_DEC_ATTN, L_LM_HEAD
 };
 
 struct AdvanceParams {
@@ -176,6 +177,7 @@ struct Launch {
   PromptTabParams pt;
   DecAttnParams da;
   AttnTokParams at;
+  LmParams lm;
   struct {
     MoeRouter R;
     int n, r, E, k, group;
@@ -335,6 +337,8 @@ static int set_kernel_attrs() {
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<128>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::kSmem));
+  CK(cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LmCfg::kSmem));
+  CK(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSampMaxVocab * 4));
   const int attn_max = 220 * 1024;
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_max));
   CK(cudaFuncSetAttribute(row_attn_kernel<__nv_bfloat16, 16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -479,6 +483,7 @@ static int run(const Launch& L, cudaStream_t st) {
              : launch_k(moe_router_kernel<float>, dim3(L.grid), dim3(L.block), L.smem, st, L.ro.R, L.ro.n, L.ro.r,
                         L.ro.E, L.ro.k, L.ro.group, L.ro.tie);
       break;
+    case L_LM_HEAD: e = launch_k(lm_head_argmax_kernel, dim3(L.grid), dim3(L.block), L.smem, st, L.lm); break;
     case L_ADVANCE: e = launch_k(advance_kernel, dim3(1), dim3(32), 0, st, L.ad); break;
     case L_NEXT_IDS: e = launch_k(next_ids_kernel, dim3(L.grid), dim3(L.block), 0, st, L.ni); break;
   }
@@ -1183,7 +1188,29 @@ static int build_final(one_engine* e, std::vector<Launch>& plan, int T, int batc
                          advance ? e->at<int>(e->b.counters) : nullptr, last_only ? seq_len : 1, last_only ? seq_len - 1 : 0};
     plan.push_back(n);
   }
-  {
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (dt == ONE_DTYPE_BF16 && Hd % 8 == 0 && a16(e->gw[ONE_G_LM_HEAD]) && a16(B_(e->b.hn))) {
+    // lm_head + argmax with the tokens as the MMA's M rows (lm_head_argmax_kernel)
+    Launch g;
+    g.kind = L_LM_HEAD;
+    g.dtype = dt;
+    LmParams& q = g.lm;
+    memset(&q, 0, sizeof(q));
+    int rc = make_map(&q.tmx, B_(e->b.hn), Tl, Hd, Hd, 128);
+    if (rc) return rc;
+    rc = make_map(&q.tmw, e->gw[ONE_G_LM_HEAD], c.vocab_size, Hd, Hd, kLmBN);
+    if (rc) return rc;
+    q.T = Tl; q.V = c.vocab_size; q.K = Hd;
+    q.t_tiles = (Tl + 127) / 128;
+    q.logits = reinterpret_cast<__nv_bfloat16*>(logits);
+    q.ldo = c.vocab_size;
+    q.best = e->at<unsigned long long>(e->b.best);
+    q.err = err;
+    g.block = LmCfg::kThreads;
+    g.smem = LmCfg::kSmem;
+    g.grid = ((c.vocab_size + kLmBN - 1) / kLmBN) * q.t_tiles;
+    plan.push_back(g);
+  } else {
     ProbSpec ps[1];
     ps[0].kind = EPI_ARGMAX; ps[0].W = e->gw[ONE_G_LM_HEAD]; ps[0].Nw = c.vocab_size; ps[0].K = Hd;
     ps[0].X = B_(e->b.hn); ps[0].ldx = Hd; ps[0].out = logits; ps[0].ldo = c.vocab_size;

@@ -418,28 +418,37 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
 
   if (warp == 0) {
     if (lane == 0) {
-      // Weights do not depend on the previous kernel: the first stages are requested before
-      // the dependency wait, so the HBM stream overlaps the previous kernel's tail.
+      // Weights do not depend on the previous kernel: the first stages are requested, and the
+      // rest of the CTA's weight slice is brought into L2, before the dependency wait. The ring
+      // refills one slot per consumed k block, so the later weight tiles then come from L2
+      // instead of costing an HBM round trip each.
       const uint64_t wpol = l2_policy_evict_first();
-      for (int i = 0; i < nkb; ++i) {
+      const int pre = min(nkb, C::kStages);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::kABytes);
+        tma_load_2d_hint(sA(i), &p.tmw[pi], &full[i], (kb0 + i) * 64, m_tile * 128, wpol);
+      }
+      for (int i = pre; i < nkb; ++i) tma_prefetch_l2_2d(&p.tmw[pi], (kb0 + i) * 64, m_tile * 128);
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % C::kStages;
         const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
-        if (i >= C::kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
+        if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
         mbar_arrive_expect_tx(&full[s], C::kABytes);
         tma_load_2d_hint(sA(s), &p.tmw[pi], &full[s], (kb0 + i) * 64, m_tile * 128, wpol);
       }
     }
-  } else if (warp == 5) {
-    // The token tiles come from another warp: one thread's bulk copies complete one after
-    // another (~0.46 us each on B200), so two issuing threads halve the stream's length.
+  } else if (warp >= 2 && warp < 2 + C::kStages) {
+    // Token tiles: one thread's bulk copies complete one after another (~0.35-0.46 us each on
+    // B200), so slot j's token tiles (k blocks j, j + S, ...) are issued by lane 0 of warp 2 + j,
+    // each in its own warp, before that warp joins the epilogue.
     if (lane == 0) {
+      const int slot = warp - 2;
       pdl_wait();
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::kStages;
+      for (int i = slot; i < nkb; i += C::kStages) {
         const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
-        if (i >= C::kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
-        mbar_arrive_expect_tx(&full[s], C::kBBytes);
-        tma_load_2d(sB(s), &p.tmx[pi], &full[s], (kb0 + i) * 64, n_tile * BN);
+        if (i >= C::kStages && !mbar_wait(&empty[slot], ph ^ 1u, p.err, 1)) break;
+        mbar_arrive_expect_tx(&full[slot], C::kBBytes);
+        tma_load_2d(sB(slot), &p.tmx[pi], &full[slot], (kb0 + i) * 64, n_tile * BN);
       }
     }
   } else if (warp == 1) {
@@ -805,6 +814,170 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtGemmParams p, 
         epi_elem<T>(P, n, t, acc[i][j], split);
       }
     }
+  }
+}
+
+}  // namespace one
+
+namespace one {
+
+// ------------------------------------------------------------------ lm_head with fused argmax
+// logits[t, v] = rnd(sum_k X[t, k] * W[v, k]) for a [T, K] activation and the [V, K] tied
+// embedding (one/modeling_one.py:902), with each token's greedy choice (the first maximum over
+// v of the rounded logits, torch.argmax) reduced into best[t] as an order-preserving 64-bit key
+// by atomicMax (argmax_key). Written only on request: the logits themselves.
+//
+// Tokens are the UMMA A operand (M = 128 token rows per tile) and a 256-row vocabulary tile is
+// B (N = 256), so TMEM lane i holds token i's 256 logits of the tile: each epilogue thread scans
+// its own row in vocabulary order and needs no cross-thread reduction. One CTA per (vocabulary
+// tile, token tile); the two token tiles of a vocabulary tile are adjacent CTAs, so the tile is
+// read from HBM once and from L2 the second time. Warp 0 streams both operands through a
+// kLmStages ring (weight tiles of the first stages before the dependency wait), warp 1 issues
+// the MMAs, warps 2..5 scan the accumulator.
+constexpr int kLmStages = 4;
+constexpr int kLmBN = 256;  // vocabulary rows per tile
+struct LmCfg {
+  static constexpr int kABytes = 128 * 64 * 2;    // token tile
+  static constexpr int kBBytes = kLmBN * 64 * 2;  // vocabulary tile
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kSmem = kLmStages * kStageBytes + 1024 + 256;
+  static constexpr int kThreads = 192;
+};
+static_assert(LmCfg::kSmem <= 227 * 1024, "lm_head shared memory");
+
+struct __align__(64) LmParams {
+  CUtensorMap tmx;  // activations [T, K], box {64, 128}
+  CUtensorMap tmw;  // weights [V, K], box {64, kLmBN}
+  int T, V, K;
+  int t_tiles;      // token tiles
+  __nv_bfloat16* logits;  // [T, ldo] or null
+  int ldo;
+  unsigned long long* best;  // [T]
+  DevErr* err;
+};
+
+__global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(const __grid_constant__ LmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kLmStages * LmCfg::kStageBytes);
+  uint64_t* empty = full + kLmStages;
+  uint64_t* accb = empty + kLmStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int v_tile = blockIdx.x / p.t_tiles, t_tile = blockIdx.x % p.t_tiles;
+  const int nkb = (p.K + 63) / 64;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kLmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kLmBN);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmx);
+    tma_prefetch_desc(&p.tmw);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  auto sA = [&](int s) { return smem + s * LmCfg::kStageBytes; };
+  auto sB = [&](int s) { return smem + s * LmCfg::kStageBytes + LmCfg::kABytes; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t wpol = l2_policy_evict_first();
+      const int pre = min(nkb, kLmStages);
+      for (int i = 0; i < pre; ++i) {  // weights: not written by earlier kernels
+        mbar_arrive_expect_tx(&full[i], LmCfg::kStageBytes);
+        tma_load_2d_hint(sB(i), &p.tmw, &full[i], i * 64, v_tile * kLmBN, wpol);
+      }
+      pdl_wait();
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % kLmStages;
+        const uint32_t ph = (uint32_t)(i / kLmStages) & 1u;
+        if (i >= pre) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 41)) break;
+          mbar_arrive_expect_tx(&full[s], LmCfg::kStageBytes);
+          tma_load_2d_hint(sB(s), &p.tmw, &full[s], i * 64, v_tile * kLmBN, wpol);
+        }
+        tma_load_2d(sA(s), &p.tmx, &full[s], i * 64, t_tile * 128);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, kLmBN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % kLmStages;
+        const uint32_t ph = (uint32_t)(i / kLmStages) & 1u;
+        if (!mbar_wait(&full[s], ph, p.err, 42)) break;
+        tc_fence_after();
+        const uint64_t ad = umma_desc_sw128(sA(s));
+        const uint64_t bd = umma_desc_sw128(sB(s));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accb);
+    }
+  } else {
+    // ---- epilogue: warp w scans TMEM lanes 32 (w % 4) .. +31 = its 32 tokens
+    pdl_wait();
+    const int q = warp & 3;
+    const int t = t_tile * 128 + q * 32 + lane;
+    const bool ok = mbar_wait(accb, 0, p.err, 43);
+    tc_fence_after();
+    uint32_t best16 = 0u;  // order-preserving bf16 bits of the best rounded logit (0: none)
+    int best_v = 0;
+    const int v0 = v_tile * kLmBN;
+    if (ok) {
+      for (int c0 = 0; c0 < kLmBN; c0 += 32) {
+        if (v0 + c0 >= p.V) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld_wait();
+        uint32_t h[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) h[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          uint32_t b = (j & 1) ? (h[j >> 1] >> 16) : (h[j >> 1] & 0xFFFFu);
+          b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+          if (v0 + c0 + j < p.V && b > best16) {  // strictly greater: the first maximum wins
+            best16 = b;
+            best_v = v0 + c0 + j;
+          }
+        }
+        if (p.logits && t < p.T) {
+          __nv_bfloat16* dst = p.logits + (size_t)t * p.ldo + v0 + c0;
+          if (v0 + c0 + 32 <= p.V && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<uint4*>(dst)[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (v0 + c0 + j < p.V)
+                dst[j] = __ushort_as_bfloat16((unsigned short)((j & 1) ? (h[j >> 1] >> 16) : (h[j >> 1] & 0xFFFFu)));
+          }
+        }
+      }
+    }
+    if (ok && t < p.T && best16)
+      atomicMax(p.best + t, ((unsigned long long)best16 << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)best_v));
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kLmBN);
   }
 }
 

@@ -71,6 +71,8 @@ SIGNATURES = {
                                          c_void_p]),
     "one_ops_error": (c_int, [POINTER(c_int32), c_int32]),
     "one_selftest_mean_division": (c_int, [c_void_p, c_int32, c_void_p, c_void_p]),
+    "one_sample_tokens": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_float, c_int32, c_float,
+                                  ctypes.c_uint64, ctypes.c_uint64, c_void_p, c_void_p]),
 }
 
 

@@ -280,15 +280,19 @@ class OneEngine:
             out = out.view(B, S, -1)
         return out
 
-    def step(self, ids: Optional[torch.Tensor] = None, logits: bool = False, next_ids: bool = True):
+    def step(self, ids: Optional[torch.Tensor] = None, logits: bool = False, next_ids: bool = True,
+             out: Optional[torch.Tensor] = None):
         """One decode step for the current batch. ids [B] (None = greedy from the previous
-        argmax). Returns (logits [B, V] or None, next_ids [B] int32 or None)."""
+        argmax). Returns (logits [B, V] or None, next_ids [B] int32 or None). `out`: a [B, V]
+        model-dtype buffer the logits are written to (reused across steps, one captured graph)."""
         B = self.batch
         idp = None
         if ids is not None:
             self._ids_buf[:B].copy_(ids.view(-1).to(torch.int32), non_blocking=True)
             idp = self._ids_buf
-        lg = torch.empty(B, self.cfg.vocab_size, dtype=self.dtype, device=self.device) if logits else None
+        lg = None
+        if logits:
+            lg = out if out is not None else torch.empty(B, self.cfg.vocab_size, dtype=self.dtype, device=self.device)
         nx = self._next_buf if next_ids else None
         C.check(C.LIB.one_engine_step(self.h, B, C.ptr(idp), C.ptr(lg), C.ptr(nx), self._stream()), "one_engine_step")
         return lg, (nx[:B] if nx is not None else None)
@@ -298,3 +302,24 @@ class OneEngine:
 
     def replay(self) -> None:
         C.check(C.LIB.one_engine_replay(self.h, self._stream()), "one_engine_replay")
+
+
+def sample_tokens(logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
+                  seed: int = 0, offset: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One token per row of logits [B, V] (CUDA, bf16 or fp32) drawn on the GPU
+    (one_sample_tokens): scores / temperature, top-k, top-p, one draw from the softmax of the
+    kept scores, as transformers' sampling loop warps its logits. The draw of row b depends on
+    (seed, offset, b) only. Returns int32 [B] on the logits' device."""
+    if logits.dim() != 2 or not logits.is_cuda:
+        raise C.OneError("sample_tokens takes CUDA logits [batch, vocab]")
+    B, V = logits.shape
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    if out is None:
+        out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    C.check(C.LIB.one_sample_tokens(C.ptr(logits), B, V, logits.stride(0), C.dtype_code(logits.dtype), float(temperature),
+                                    int(top_k or 0), float(1.0 if top_p is None else top_p),
+                                    ctypes.c_uint64(seed & (2 ** 64 - 1)), ctypes.c_uint64(offset & (2 ** 64 - 1)),
+                                    C.ptr(out), ctypes.c_void_p(torch.cuda.current_stream(logits.device).cuda_stream)),
+            "one_sample_tokens")
+    return out

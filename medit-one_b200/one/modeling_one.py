@@ -228,6 +228,88 @@ class OneForCausalLM(OnePreTrainedModel, GenerationMixin):
         return CausalLMOutputWithPast(loss=loss, logits=logits, past_key_values=cache)
 
     @torch.no_grad()
+    def generate(self, input_ids: Optional[torch.LongTensor] = None, generation_config=None, max_length=None,
+                 max_new_tokens=None, do_sample=None, temperature=None, top_k=None, top_p=None, eos_token_id=None,
+                 pad_token_id=None, seed: Optional[int] = None, attention_mask=None, **kwargs) -> torch.LongTensor:
+        """GenerationMixin.generate for greedy search and multinomial sampling, run on the engine
+        (the reference's documented use, README.md:73, model.generate(input_ids, max_length=50,
+        temperature=0.7), goes through transformers' generation loop, one/modeling_one.py:845).
+
+        Arguments resolve as transformers resolves them: explicit argument, else the model's
+        generation_config, else the default (do_sample False, temperature 1, no top-k, top_p 1,
+        max_length 20). do_sample=False is greedy search whatever the temperature (the
+        argmax fused into lm_head, steps replayed from a captured graph); do_sample=True warps
+        each step's logits (temperature, top-k, top-p) and draws one token per sequence on the
+        GPU (one_sample_tokens). Once a sequence emits eos_token_id its later tokens are
+        pad_token_id (eos when pad is unset), and generation stops when every sequence has
+        finished. `seed` fixes the draws (default: drawn from torch's global generator).
+        Returns [B, S + new tokens]. Beam search, constraints and streaming are not supported."""
+        unsupported = {k: v for k, v in kwargs.items()
+                       if v is not None and not (k in ("num_beams", "num_return_sequences") and v == 1)
+                       and k not in ("use_cache", "return_dict_in_generate", "output_scores", "output_logits")}
+        if unsupported or kwargs.get("return_dict_in_generate") or kwargs.get("output_scores"):
+            raise NotImplementedError(f"generate() on the B200 engine does not support {sorted(unsupported or kwargs)}")
+        gc = generation_config if generation_config is not None else getattr(self, "generation_config", None)
+
+        def pick(v, name, default):
+            if v is not None:
+                return v
+            g = getattr(gc, name, None) if gc is not None else None
+            return g if g is not None else default
+
+        do_sample = bool(pick(do_sample, "do_sample", False))
+        temperature = float(pick(temperature, "temperature", 1.0))
+        top_k = int(pick(top_k, "top_k", 0) or 0)
+        top_p = float(pick(top_p, "top_p", 1.0))
+        eos = pick(eos_token_id, "eos_token_id", None)
+        if isinstance(eos, (list, tuple)):
+            if len(eos) > 1:
+                raise NotImplementedError("one eos_token_id")
+            eos = eos[0] if eos else None
+        pad = pick(pad_token_id, "pad_token_id", None)
+        if pad is None:
+            pad = eos
+        if input_ids is None:
+            raise ValueError("generate() needs input_ids")
+        B, S = input_ids.shape
+        if max_new_tokens is None:
+            max_new_tokens = int(pick(max_length, "max_length", 20)) - S
+        if max_new_tokens <= 0:
+            return input_ids
+        if do_sample and not temperature > 0:
+            raise ValueError("do_sample=True needs temperature > 0")
+        eng = self.engine(max_batch=B, max_tokens=max(B * S, B), max_positions=S + max_new_tokens + 16)
+        if not do_sample:
+            if eng.hist_cap < max_new_tokens:
+                raise ValueError(f"max_new_tokens > engine history capacity ({eng.hist_cap})")
+            eng.prefill(input_ids)
+            for _ in range(max_new_tokens):
+                eng.step(None, next_ids=False)
+            new = eng.history(max_new_tokens, B).t().to(torch.long)
+        else:
+            from .engine import sample_tokens
+            if seed is None:
+                seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+            lg = eng.prefill(input_ids, logits="last")
+            buf = torch.empty(B, self.config.vocab_size, dtype=lg.dtype, device=lg.device)
+            toks = torch.empty(max_new_tokens, B, dtype=torch.int32, device=lg.device)
+            for i in range(max_new_tokens):
+                sample_tokens(lg, temperature, top_k, top_p, seed, i, out=toks[i])
+                if i + 1 < max_new_tokens:
+                    lg, _ = eng.step(toks[i], logits=True, next_ids=False, out=buf)
+            new = toks.t().to(torch.long)
+        if eos is not None:
+            # tokens after a sequence's first eos become pad; stop once all have finished
+            hit = new == int(eos)
+            after = (hit.cumsum(1) - hit.long()) > 0
+            new = torch.where(after, torch.full_like(new, int(pad)), new)
+            done = hit.cumsum(1) > 0
+            all_done = done.all(0)
+            if bool(all_done.any()):
+                new = new[:, : int(all_done.nonzero()[0]) + 1]
+        return torch.cat([input_ids.to(new.device), new], dim=1)
+
+    @torch.no_grad()
     def generate_greedy(self, input_ids: torch.LongTensor, max_new_tokens: int) -> torch.LongTensor:
         """Greedy decode on the engine: prompt ingestion, then max_new_tokens single-token steps
         with the argmax fed back on the device. Returns [B, S + max_new_tokens]."""
