@@ -754,7 +754,8 @@ def profile_case(args):
     torch.cuda.synchronize()
     if eng.device_error() != (0, 0):
         raise RuntimeError(f"device error {eng.device_error()}")
-    print(json.dumps({"profile_case": "ok", "launches_per_step": eng.step_launches(BATCH)}))
+    print(json.dumps({"profile_case": "ok", "launches_per_step": eng.step_launches(BATCH),
+                      "prefill_launches": eng.prefill_launches(BATCH, 16)}))
 
 
 def profile_prefill(args):

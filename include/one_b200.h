@@ -146,10 +146,12 @@ int one_linear_moe(const void* x, int32_t n, int32_t fin, int32_t fout, const vo
  * memory: a host program that binds this library through a foreign-function interface and only
  * holds the device pointers it is handed, or a process whose device memory belongs entirely to
  * another runtime's pool. No counterpart in the reference. The scratch is a static array in the
- * library image of ONE_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library
- * until the process exits; calls needing more (n * fin too large) fail with ONE_ERR_INVALID.
- * The first call on a device looks the array's device address up (cudaGetSymbolAddress) with
- * that device current, so make that first call before any stream capture; a call made after a
+ * library image of ONE_NOALLOC_SCRATCH_BYTES per GPU; calls needing more (n * fin too large)
+ * fail with ONE_ERR_INVALID. The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress) with that device current; with CUDA's lazy module loading that lookup
+ * is also when the array takes its device memory, which the GPU then holds until the process
+ * exits. Make that first call before any stream capture (and, if the caller's memory is
+ * budgeted, before the budget is fixed); a call made after a
  * cudaDeviceReset (a new context) looks it up again. Every call shares the
  * one array: calls whose work overlaps on the GPU (other streams, other host threads) race;
  * serialise them. No call allocates or frees device memory. */

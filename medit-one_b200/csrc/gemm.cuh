@@ -170,16 +170,18 @@ struct TcCfg {
 // each packed add / multiply of bf16 operands is one rounding of the exact result, so the
 // values equal the fp32-then-round sequence of one/modeling_one.py:559-565 and
 // one/linear_moe.py:53.
-ONE_DEVINL void epi_packed8(int kind, const float (&a)[8], const uint4& aux, __nv_bfloat16* out, __nv_bfloat16* out2) {
+// `st` false computes without storing (the epilogue's instruction-cache warm-up pass).
+ONE_DEVINL void epi_packed8(int kind, const float (&a)[8], const uint4& aux, __nv_bfloat16* out, __nv_bfloat16* out2,
+                            bool st = true) {
   uint32_t y[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) y[j] = pack_bf16x2(a[2 * j], a[2 * j + 1]);
   if (kind == EPI_CX) {
-    *reinterpret_cast<uint4*>(out) = make_uint4(y[0], y[1], y[2], y[3]);
+    if (st) *reinterpret_cast<uint4*>(out) = make_uint4(y[0], y[1], y[2], y[3]);
     uint32_t z[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) z[j] = bf2_min(bf2_max(y[j], 0xc61cc61cu), 0x461c461cu);  // +-9984
-    *reinterpret_cast<uint4*>(out2) = make_uint4(z[0], z[1], z[2], z[3]);
+    if (st) *reinterpret_cast<uint4*>(out2) = make_uint4(z[0], z[1], z[2], z[3]);
     return;
   }
   const uint32_t x[4] = {aux.x, aux.y, aux.z, aux.w};
@@ -187,7 +189,7 @@ ONE_DEVINL void epi_packed8(int kind, const float (&a)[8], const uint4& aux, __n
   if (kind == EPI_RESID) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = bf2_add(x[j], y[j]);
-    *reinterpret_cast<uint4*>(out) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (st) *reinterpret_cast<uint4*>(out) = make_uint4(o[0], o[1], o[2], o[3]);
     return;
   }
 #pragma unroll
@@ -195,7 +197,7 @@ ONE_DEVINL void epi_packed8(int kind, const float (&a)[8], const uint4& aux, __n
     const uint32_t cl = bf2_min(bf2_max(y[j], 0xc2c8c2c8u), 0x42c842c8u);  // +-100
     o[j] = kind == EPI_HXPRE ? bf2_add(x[j], cl) : bf2_mul(x[j], cl);
   }
-  *reinterpret_cast<uint4*>(out) = make_uint4(o[0], o[1], o[2], o[3]);
+  if (st) *reinterpret_cast<uint4*>(out) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 template <int BN>
@@ -238,14 +240,27 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
     }
   };
   aux_load(0);
-  const bool ok = mbar_wait(accb, 0, p.err, 3);
-  tc_fence_after();
+  // Two passes over the same code. Pass 0 runs on warps 2..5 while the MMAs are still in flight,
+  // with the TMEM reads and every global store switched off: it only brings this code into the
+  // instruction cache, where a cold epilogue otherwise spent about a microsecond missing after
+  // the accumulator was ready. Pass 1 is the epilogue proper, on all six warps.
+  bool ok = true;
+#pragma unroll 1
+  for (int pass = drain ? 0 : 1; pass < 2; ++pass) {
+  const bool dry = pass == 0;
+  const int nt = dry ? 128 : NT;  // threads of the pass's named barrier
+  const int bar = dry ? 2 : 1;    // its own barrier: warps 0 and 1 may already wait on barrier 1
+  if (!dry) {
+    ok = mbar_wait(accb, 0, p.err, 3);
+    tc_fence_after();
+  }
   for (int cc = 0; cc < BN; cc += CH) {
     const int tn = min(CH, P.T - (t_tile + cc));
     if (tn <= 0) break;
-    if (cc > 0) aux_load(cc);
+    if (cc > 0 && !dry) aux_load(cc);
     // ---- E1
     if (kind == EPI_ARGMAX) {
+      if (dry) break;
       // per token: max over this warp's 32 rows of a 32-bit key (order-preserving bf16 bits,
       // then 255 - row in tile, so equal values keep the lowest row), one redux per token;
       // the four warps' keys meet in S, then one 64-bit atomicMax per token and CTA.
@@ -291,12 +306,14 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
       for (int c0 = 0; c0 < CH; c0 += 16) {
         if (c0 >= tn) break;  // warp-uniform
         float v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc + c0), v);
-        tmem_ld_wait();
+        if (!dry) {
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc + c0), v);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
+          for (int j = 0; j < 16; ++j) S[(c0 + j) * 128 + q * 32 + lane] = v[j];
+        }
       }
-    named_barrier_sync(1, NT);
+    named_barrier_sync(bar, nt);
     // ---- E2
     const int tb = t_tile + cc;
     if (false) {
@@ -315,7 +332,8 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
           const uint32_t u2 = pack_bf16x2(sv[4 * j + 1] + bg[4 * j + 1], sv[4 * j + 3] + bg[4 * j + 3]);
           o4[j] = bf2_mul(pack_bf16x2(gelu_erf(bf2_lo(g2)), gelu_erf(bf2_hi(g2))), u2);
         }
-        *reinterpret_cast<uint4*>(out + (size_t)(tb + tl) * P.ldo + (ng >> 1)) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+        if (!dry)
+          *reinterpret_cast<uint4*>(out + (size_t)(tb + tl) * P.ldo + (ng >> 1)) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
       }
     } else {
 #pragma unroll
@@ -330,20 +348,21 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
           a[0] = f0.x; a[1] = f0.y; a[2] = f0.z; a[3] = f0.w; a[4] = f1.x; a[5] = f1.y; a[6] = f1.z; a[7] = f1.w;
         }
         if (kind == EPI_PARTIAL) {
-          store8(P.ws + ((size_t)split * P.T + t) * P.ldw + n0, a);
+          if (!dry) store8(P.ws + ((size_t)split * P.T + t) * P.ldw + n0, a);
           continue;
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) a[j] += b8[j];
         T* out = reinterpret_cast<T*>(P.out) + (size_t)t * P.ldo + n0;
         if (kind == EPI_STORE) {
-          store8(out, a);
+          if (!dry) store8(out, a);
         } else {
-          epi_packed8(kind, a, auxr[k], out, reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0);
+          epi_packed8(kind, a, auxr[k], out, reinterpret_cast<T*>(P.out2) + (size_t)t * P.ldo2 + n0, !dry);
         }
       }
     }
-    named_barrier_sync(1, NT);
+    named_barrier_sync(bar, nt);
+  }
   }
 }
 
@@ -393,7 +412,7 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 2);  // the weight copy and the token copy of the slot arrive
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accb, 1);
@@ -425,30 +444,20 @@ __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_const
       const uint64_t wpol = l2_policy_evict_first();
       const int pre = min(nkb, C::kStages);
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], C::kABytes);
+        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
         tma_load_2d_hint(sA(i), &p.tmw[pi], &full[i], (kb0 + i) * 64, m_tile * 128, wpol);
       }
       for (int i = pre; i < nkb; ++i) tma_prefetch_l2_2d(&p.tmw[pi], (kb0 + i) * 64, m_tile * 128);
-      for (int i = pre; i < nkb; ++i) {
+      pdl_wait();
+      for (int i = 0; i < nkb; ++i) {
         const int s = i % C::kStages;
         const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
-        mbar_arrive_expect_tx(&full[s], C::kABytes);
-        tma_load_2d_hint(sA(s), &p.tmw[pi], &full[s], (kb0 + i) * 64, m_tile * 128, wpol);
-      }
-    }
-  } else if (warp >= 2 && warp < 2 + C::kStages) {
-    // Token tiles: one thread's bulk copies complete one after another (~0.35-0.46 us each on
-    // B200), so slot j's token tiles (k blocks j, j + S, ...) are issued by lane 0 of warp 2 + j,
-    // each in its own warp, before that warp joins the epilogue.
-    if (lane == 0) {
-      const int slot = warp - 2;
-      pdl_wait();
-      for (int i = slot; i < nkb; i += C::kStages) {
-        const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
-        if (i >= C::kStages && !mbar_wait(&empty[slot], ph ^ 1u, p.err, 1)) break;
-        mbar_arrive_expect_tx(&full[slot], C::kBBytes);
-        tma_load_2d(sB(slot), &p.tmx[pi], &full[slot], (kb0 + i) * 64, n_tile * BN);
+        if (i >= pre) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 1)) break;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          tma_load_2d_hint(sA(s), &p.tmw[pi], &full[s], (kb0 + i) * 64, m_tile * 128, wpol);
+        }
+        tma_load_2d(sB(s), &p.tmx[pi], &full[s], (kb0 + i) * 64, n_tile * BN);
       }
     }
   } else if (warp == 1) {
@@ -868,7 +877,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
   const int nkb = (p.K + 63) / 64;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kLmStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // the weight copy and the token copy of the slot arrive
       mbar_init(&empty[s], 1);
     }
     mbar_init(accb, 1);
@@ -890,27 +899,33 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
   auto sA = [&](int s) { return smem + s * LmCfg::kStageBytes; };
   auto sB = [&](int s) { return smem + s * LmCfg::kStageBytes + LmCfg::kABytes; };
 
-  if (warp == 0) {
+  if (warp >= 2 && warp < 2 + kLmStages) {
+    // TMA issue, one thread per slot: one thread's bulk copies complete one after another
+    // (~0.4 us each on B200), so lane 0 of warp 2 + j loads both operands of the k blocks j,
+    // j + S, ... (S = kLmStages) before the warp turns to the epilogue. Weight tiles are not
+    // written by earlier kernels: each slot's first one is requested before the dependency wait.
     if (lane == 0) {
+      const int slot = warp - 2;
       const uint64_t wpol = l2_policy_evict_first();
-      const int pre = min(nkb, kLmStages);
-      for (int i = 0; i < pre; ++i) {  // weights: not written by earlier kernels
-        mbar_arrive_expect_tx(&full[i], LmCfg::kStageBytes);
-        tma_load_2d_hint(sB(i), &p.tmw, &full[i], i * 64, v_tile * kLmBN, wpol);
+      if (slot < nkb) {
+        mbar_arrive_expect_tx(&full[slot], LmCfg::kBBytes);
+        tma_load_2d_hint(sB(slot), &p.tmw, &full[slot], slot * 64, v_tile * kLmBN, wpol);
       }
       pdl_wait();
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % kLmStages;
+      for (int i = slot; i < nkb; i += kLmStages) {
         const uint32_t ph = (uint32_t)(i / kLmStages) & 1u;
-        if (i >= pre) {
-          if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 41)) break;
-          mbar_arrive_expect_tx(&full[s], LmCfg::kStageBytes);
-          tma_load_2d_hint(sB(s), &p.tmw, &full[s], i * 64, v_tile * kLmBN, wpol);
+        if (i >= kLmStages) {
+          if (!mbar_wait(&empty[slot], ph ^ 1u, p.err, 41)) break;
+          mbar_arrive_expect_tx(&full[slot], LmCfg::kBBytes);
+          tma_load_2d_hint(sB(slot), &p.tmw, &full[slot], i * 64, v_tile * kLmBN, wpol);
         }
-        tma_load_2d(sA(s), &p.tmx, &full[s], i * 64, t_tile * 128);
+        mbar_arrive_expect_tx(&full[slot], LmCfg::kABytes);
+        tma_load_2d(sA(slot), &p.tmx, &full[slot], i * 64, t_tile * 128);
       }
     }
-  } else if (warp == 1) {
+    __syncwarp();
+  }
+  if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(128, kLmBN);
       for (int i = 0; i < nkb; ++i) {
@@ -926,7 +941,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
       }
       umma_commit(accb);
     }
-  } else {
+  } else if (warp >= 2) {
     // ---- epilogue: warp w scans TMEM lanes 32 (w % 4) .. +31 = its 32 tokens
     pdl_wait();
     const int q = warp & 3;
