@@ -42,6 +42,13 @@ SEED = 4
 METRIC = "decode tok/s (140M-class bf16, B=256 per GPU)"
 
 
+# DRAM bytes measured by ncu (read + write) for the bench workloads' dominant kernels, per launch:
+# one graph-replayed decode step of the 140M bf16 model at 256 sequences (the 76 launches summed,
+# caches left warm: 304.3 MB read + 44.8 MB written) and one non-causal [8, 12, 2048, 64]
+# attention launch (103.7 MB; algorithmic q, k, v, out = 100.7 MB).
+STEP_DRAM_BYTES = {256: 349.05e6}
+ATTN_DRAM_BYTES = 103.7e6
+
 def peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
@@ -329,7 +336,10 @@ def run_native(args, ws, rank, local):
                        "l2": "inputs larger than L2 (285 MB of weights streamed per step)"},
             "roofline": {"bound": "hbm", "kernel": f"decode step ({launches} launches, CUDA graph)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "peak_source": src, "traffic": None, "algorithmic_bytes_per_step": sb["total"],
+                         "peak_source": src, "traffic": STEP_DRAM_BYTES.get(bl),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed over the "
+                                           "76 launches of one decode step (--cache-control none, serialized)",
+                         "algorithmic_bytes_per_step": sb["total"],
                          "tflops_achieved": sb["flops"] / t_step / 1e12,
                          "tensor_frac_sustained": sb["flops"] / t_step / 1e12 / tf_sus},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": bl * 4, "d2h_bytes_per_step": bl * 4},
@@ -467,7 +477,9 @@ def run_attention(args, ws, rank, local):
                            "l2": "256 MB buffer written between timed calls (inputs 75 MB < L2)"},
                 "roofline": {"bound": "tensor", "kernel": "flash_attn_tc_kernel + rope_qk_kernel",
                              "achieved": value / ws, "peak": tf, "unit": "TFLOP/s", "frac": value / ws / tf,
-                             "peak_source": src, "traffic": None},
+                             "peak_source": src, "traffic": ATTN_DRAM_BYTES,
+                             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one non-causal "
+                                               "flash_attn_tc_kernel launch (L2 flushed first)"},
                 "e2e": {"value": e2e, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "gpu_launches": 4 * args.steps, "clocks": clocks}
         if ws == 1 and not args.no_cpu_baseline:

@@ -207,6 +207,9 @@ static int pick_bn(int T, int m_tiles_total) {
     const int ctas = m_tiles_total * ((T + bn - 1) / bn);
     if (bn <= T * 2 && ctas >= num_sms()) return bn;
   }
+  // a launch that leaves SMs idle at 64-token tiles: 32-token tiles halve each CTA's epilogue
+  // (its MMA chain, K / 16 MMAs, does not depend on the tile width)
+  if (m_tiles_total * ((T + 63) / 64) < num_sms()) return 32;
   return T > 32 ? 64 : 32;
 }
 
