@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define ONE_B200_ABI_VERSION 1
+#define ONE_B200_ABI_VERSION 2
 
 enum { ONE_OK = 0, ONE_ERR_INVALID = 1, ONE_ERR_CUDA = 2, ONE_ERR_UNSUPPORTED = 3, ONE_ERR_DEVICE = 4 };
 enum { ONE_DTYPE_BF16 = 0, ONE_DTYPE_F32 = 1 };
@@ -53,6 +53,12 @@ typedef struct one_config {
   int32_t dtype;
   float rms_norm_eps;
   float rope_theta;
+  /* OneConfig.use_flash_attention (one/modeling_one.py:295-310, 408-421) with the reference's
+   * turbo semantics (TurboFlashAttention(causal=True), one/turbo_ops.py:437-475): per head,
+   * causal softmax attention across the call's tokens over the lin_q / lin_k / lin_v outputs
+   * (head dim = num_attention_heads, scale 1/sqrt(num_attention_heads)); a one-token decode
+   * call therefore sees only its own token and its attention output is lin_v(value). */
+  int32_t use_flash_attention;
 } one_config;
 
 /* Per-layer weight slots (names of the reference parameters, one/modeling_one.py:231-292,

@@ -23,6 +23,14 @@ namespace one {
 
 constexpr int kTokWarps = 8;
 
+// What attn_token_warp produces for a token (one/modeling_one.py:408-547):
+//   kAttnFeature  the feature attention o = softmax(q * k) * v per head (use_flash_attention off)
+//   kAttnValue    o = v: the flash-attention path over a call of one token, whose causal
+//                 attention sees that token only, so the softmax weight is exactly 1
+//   kAttnQKV      the projected q | k | v rows themselves ([3][H][H] bf16, bias added), for the
+//                 flash-attention path's causal attention across the call's tokens
+enum : int { kAttnFeature = 0, kAttnValue = 1, kAttnQKV = 2 };
+
 struct AttnTokParams {
   int T, H, seq_len;
   const __nv_bfloat16* rope;  // [seq_len][Dh]: cos(f_i) for i < Dh/2, then sin(f_i); f_i = inv_freq_i * (pos0 + s)
@@ -31,8 +39,10 @@ struct AttnTokParams {
   uint32_t scale2;            // the scale as bf16x2, when scale_exact (a bf16 value)
   int scale_exact;
   const __nv_bfloat16 *wq, *bq, *wk, *bk, *wv, *bv;  // lin_q / lin_k / lin_v [H, Dh], [H]
-  __nv_bfloat16* out;         // [T][H * H]
+  __nv_bfloat16* out;         // [T][H * H] (mode kAttnQKV: [T][out_ld] rows of q | k | v, 3 H * H each)
   uint32_t clamp2;            // bf16x2 bound of the LinearMoE input clamp (0: store o unclamped)
+  int mode;                   // kAttnFeature or kAttnQKV
+  int out_ld;                 // elements per output row
 };
 
 // Per-position tables of one prompt call, shared by all layers: the RoPE cos / sin
@@ -70,7 +80,7 @@ struct AttnTokSmem {
   static constexpr int BIAS = 3 * 16 * RS * 2;
   static constexpr int WARP0 = BIAS + 3 * 16 * 4;
   __host__ __device__ static int rows_bytes(int H) { return 3 * H * RS * 2; }
-  __host__ __device__ static int per_warp(int H) { return (2 * rows_bytes(H) + H * H * 2 + 15) & ~15; }
+  __host__ __device__ static int per_warp(int H) { return (2 * rows_bytes(H) + 3 * H * H * 2 + 15) & ~15; }
   __host__ __device__ static int total(int H) { return WARP0 + kTokWarps * per_warp(H); }
 };
 
@@ -124,11 +134,11 @@ ONE_DEVINL void load_token_rows(const __nv_bfloat16* src_row, int H, __nv_bfloat
 //
 // One token by one warp: rows = the token's q | k | v ([3H][RS] bf16), ws / bs the staged
 // projections; writes the output row (clamped to +-clamp2 when clamp2 != 0) as bf16 pairs
-// into stage[H*H/2].
+// into stage[H*H/2], or with mode kAttnQKV the unclamped q | k | v rows into stage[3*H*H/2].
 template <int DH>
 ONE_DEVINL void attn_token_warp(const __nv_bfloat16* rows, const uint2 (&cs)[DH / 32], const uint2 (&sn)[DH / 32],
                                 const __nv_bfloat16* ws, const float* bs, int H, float scale, uint32_t scale2,
-                                int scale_exact, uint32_t clamp2, uint32_t* stage) {
+                                int scale_exact, uint32_t clamp2, uint32_t* stage, int mode = kAttnFeature) {
   constexpr int RS = DH + 16, NS = DH / 16;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const bool two_nt = H > 8;
@@ -206,7 +216,19 @@ ONE_DEVINL void attn_token_warp(const __nv_bfloat16* rows, const uint2 (&cs)[DH 
       vv[nt] = pack_bf16x2(acc[2][nt][2 * rr] + bs[32 + j], acc[2][nt][2 * rr + 1] + bs[32 + j + 1]);
       const uint32_t m = (j < H ? 0u : 0xffffu) | (j + 1 < H ? 0u : 0xffff0000u);
       lg[nt] = (bf2_mul(q2, k2) & ~m) | (0xff80ff80u & m);  // masked outputs: -inf
+      if (mode != kAttnFeature && h < H && j < H) {
+        if (mode == kAttnQKV) {
+          stage[(h * H + j) >> 1] = q2;
+          stage[(H * H + h * H + j) >> 1] = k2;
+          stage[(2 * H * H + h * H + j) >> 1] = vv[nt];
+        } else {
+          uint32_t o2 = vv[nt];
+          if (clamp2) o2 = bf2_min(bf2_max(o2, negc), clamp2);  // LinearMoE clamp (one/linear_moe.py:53)
+          stage[(h * H + j) >> 1] = o2;
+        }
+      }
     }
+    if (mode != kAttnFeature) continue;  // warp-uniform
     uint32_t m2 = bf2_max(lg[0], lg[1]);
     float mx = fmaxf(bf2_lo(m2), bf2_hi(m2));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -289,10 +311,11 @@ __global__ void __launch_bounds__(kTokWarps * 32, 2) attn_tok_kernel(const AttnT
       sn[ls] = *reinterpret_cast<const uint2*>(tab + HALF + ls * 16 + 4 * c);
     }
     __syncwarp();
-    attn_token_warp<DH>(rows, cs, sn, ws, bs, H, p.scale, p.scale2, p.scale_exact, p.clamp2, stage);
+    attn_token_warp<DH>(rows, cs, sn, ws, bs, H, p.scale, p.scale2, p.scale_exact, p.clamp2, stage, p.mode);
     __syncwarp();
-    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (size_t)t * HH);
-    for (int w = lane; w < HH / 2; w += 32) dst[w] = stage[w];
+    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (size_t)t * p.out_ld);
+    const int nw = (p.mode == kAttnQKV ? 3 * HH : HH) / 2;
+    for (int w = lane; w < nw; w += 32) dst[w] = stage[w];
     __syncwarp();  // buffer it & 1 is refilled by the next iteration's issue
   }
   cp_async_wait<0>();

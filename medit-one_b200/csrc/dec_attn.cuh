@@ -37,6 +37,7 @@ struct DecAttnParams {
   MoeRouter rt[3];       // hx_moe, x_moe (gate_w [r, H*H]), cx_moe (glog precomputed, x = clamp(cx))
   unsigned long long tie;
   DevErr* err;
+  int mode;              // kAttnFeature, or kAttnValue (use_flash_attention: o = v for a one-token call)
 };
 
 // Shared memory (byte offsets).
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) dec_attn_kernel(const DecAttnP
           sn[ls] = *reinterpret_cast<const uint2*>(tab + DH / 2 + ls * 16 + 4 * c);
         }
         __syncwarp();
-        attn_token_warp<DH>(rows, cs, sn, ws, bs, H, p.scale, p.scale2, p.scale_exact, 0x461c461cu, stage);
+        attn_token_warp<DH>(rows, cs, sn, ws, bs, H, p.scale, p.scale2, p.scale_exact, 0x461c461cu, stage, p.mode);
         __syncwarp();
         for (int w = lane; w < HH / 2; w += 32) {
           const uint32_t u = stage[w];

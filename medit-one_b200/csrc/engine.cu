@@ -37,6 +37,7 @@
 #include "router.cuh"
 #include "dec_attn.cuh"
 #include "sample.cuh"
+#include "seq_attn.cuh"
 
 using namespace one;
 
@@ -119,7 +120,7 @@ struct ProbSpec {
 
 enum LaunchKind {
   L_GEMM_TC, L_GEMM_SIMT, L_ROW_PRE, L_ROW_ATTN, L_SCAN, L_ROW_NORM, L_ADVANCE, L_NEXT_IDS,
-  L_PROMPT_TAB, L_ATTN_TOK, L_ROUTER, L_ROW_PRE_W, L_DEC_ATTN, L_LM_HEAD
+  L_PROMPT_TAB, L_ATTN_TOK, L_ROUTER, L_ROW_PRE_W, L_DEC_ATTN, L_LM_HEAD, L_SEQ_ATTN
 };
 
 struct AdvanceParams {
@@ -177,6 +178,7 @@ struct Launch {
   PromptTabParams pt;
   DecAttnParams da;
   AttnTokParams at;
+  SeqAttnParams sa;
   LmParams lm;
   struct {
     MoeRouter R;
@@ -467,6 +469,9 @@ static int run(const Launch& L, cudaStream_t st) {
         default: e = launch_k(attn_tok_kernel<64>, dim3(L.grid), dim3(L.block), L.smem, st, L.at); break;
       }
       break;
+    case L_SEQ_ATTN:
+      e = launch_k(seq_attn_kernel, dim3(L.grid, L.sa.H, L.nv), dim3(kSeqQ), 0, st, L.sa);
+      break;
     case L_ROUTER:
       if (L.ro.np > 0) {
         switch (L.ro.np) {
@@ -715,6 +720,10 @@ static int check_cfg(const one_config& c) {
   if (c.num_experts < 0 || c.num_experts > kMaxExperts) return fail(ONE_ERR_UNSUPPORTED, "at most %d experts", kMaxExperts);
   if (c.num_experts > 0 && (c.top_k < 1 || c.r < 1)) return fail(ONE_ERR_INVALID, "top_k and r must be positive");
   if (c.intermediate_size % 8) return fail(ONE_ERR_UNSUPPORTED, "intermediate_size must be a multiple of 8");
+  if (c.use_flash_attention && !(dec_attn_eligible(c) && attn_tok_eligible(c) && c.num_attention_heads <= kSeqMaxH))
+    return fail(ONE_ERR_UNSUPPORTED,
+                "use_flash_attention is built for bf16 models with routed LinearMoE layers, an even number of heads "
+                "<= %d and head_dim 32 or 64", kSeqMaxH);
   return ONE_OK;
 }
 
@@ -961,6 +970,8 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       r2.idx_out = ridx + (size_t)2 * T * k;
       q.tie = topk_tie_selection(c.num_experts, std::min(c.top_k, c.num_experts));
       q.err = err;
+      // use_flash_attention: the causal attention of a one-token call sees that token only
+      q.mode = c.use_flash_attention ? kAttnValue : kAttnFeature;
       plan.push_back(a);
     } else if (tok) {
       Launch a;
@@ -985,6 +996,15 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       q.out = e->at<__nv_bfloat16>(e->b.o);
       // bf16(1e4) = 9984: the clamp bound of a bf16 tensor
       q.clamp2 = moe ? 0x461c461cu : 0u;
+      q.mode = kAttnFeature;
+      q.out_ld = HH;
+      if (c.use_flash_attention) {
+        // q | k | v of each token written over its own (already consumed) projection row,
+        // then the causal attention across each prompt's tokens writes o
+        q.mode = kAttnQKV;
+        q.out = e->at<__nv_bfloat16>(e->b.proj);
+        q.out_ld = 3 * HD;
+      }
       a.smem = Dh == 32 ? AttnTokSmem<32>::total(H) : AttnTokSmem<64>::total(H);
       int per_sm = 1;
       cudaError_t oe = Dh == 32 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_tok_kernel<32>, a.block, a.smem)
@@ -992,6 +1012,19 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
       if (oe != cudaSuccess || per_sm < 1) return fail(ONE_ERR_CUDA, "attention kernel does not fit an SM");
       a.grid = std::max(1, std::min((T + kTokWarps - 1) / kTokWarps, num_sms() * per_sm));
       plan.push_back(a);
+      if (c.use_flash_attention) {
+        if (H > kSeqMaxH || seq_len < 1 || T != batch * seq_len)
+          return fail(ONE_ERR_UNSUPPORTED, "flash attention: at most %d heads", kSeqMaxH);
+        Launch sq;
+        sq.kind = L_SEQ_ATTN;
+        sq.dtype = dt;
+        sq.grid = (seq_len + kSeqQ - 1) / kSeqQ;
+        sq.nv = batch;
+        sq.block = kSeqQ;
+        sq.sa = SeqAttnParams{e->at<__nv_bfloat16>(e->b.proj), 3 * HD, e->at<__nv_bfloat16>(e->b.o), seq_len, H,
+                              1.0f / sqrtf((float)H), moe ? 9984.0f : 0.0f};
+        plan.push_back(sq);
+      }
       if (moe) {
         ProbSpec ps[2];
         ps[0].W = LW(ONE_W_HX_GATE); ps[0].Nw = c.r; ps[0].K = HH; ps[0].X = B_(e->b.o); ps[0].ldx = HH;
@@ -1022,8 +1055,10 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
         }
       }
     } else {
+      if (c.use_flash_attention)
+        return fail(ONE_ERR_UNSUPPORTED, "use_flash_attention needs the bf16 warp-per-token / decode attention kernels");
       Launch a;
-      a.kind = L_ROW_ATTN;
+            a.kind = L_ROW_ATTN;
       a.dtype = dt;
       a.block = kAttnThreads;
       a.grid = std::min((T + kAttnTok - 1) / kAttnTok, num_sms() * 2);

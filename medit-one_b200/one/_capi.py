@@ -29,7 +29,8 @@ class OneConfigC(ctypes.Structure):
     _fields_ = [(n, c_int32) for n in ("vocab_size", "hidden_size", "transformer_dim", "num_hidden_layers",
                                        "num_attention_heads", "head_dim", "intermediate_size", "num_experts",
                                        "top_k", "r", "mlp_bias", "dtype")] + [("rms_norm_eps", c_float),
-                                                                              ("rope_theta", c_float)]
+                                                                              ("rope_theta", c_float),
+                                                                              ("use_flash_attention", c_int32)]
 
 
 # name -> (restype, argtypes); exactly the functions declared in include/one_b200.h
@@ -80,6 +81,10 @@ class OneError(RuntimeError):
     pass
 
 
+# ONE_B200_ABI_VERSION of include/one_b200.h that the structures above follow
+ABI_VERSION = 2
+
+
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(f"libone_b200.so not found at {LIB_PATH}; build it with `python medit-one_b200/build.py`")
@@ -88,6 +93,9 @@ def _load():
         fn = getattr(lib, name)  # AttributeError if a declared symbol is missing
         fn.restype = res
         fn.argtypes = args
+    if lib.one_abi_version() != ABI_VERSION:
+        raise ImportError(f"{LIB_PATH} has ABI version {lib.one_abi_version()}, this package needs {ABI_VERSION}; "
+                          "rebuild it with `python medit-one_b200/build.py`")
     return lib
 
 

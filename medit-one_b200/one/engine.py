@@ -62,26 +62,27 @@ def prompt_divisors(seq_len: int, dtype: torch.dtype) -> torch.Tensor:
     return (torch.arange(1, seq_len + 1, dtype=dtype) + 1e-10).float()
 
 
-def check_supported(config) -> None:
+def check_supported(config, dtype=torch.bfloat16) -> None:
     """Raise NotImplementedError for OneConfig switches whose reference behaviour the engine
     does not compute, instead of silently running the default path.
 
+    * ``use_single_token=True`` computes the attention of each sequence's last position only
+      and broadcasts it over the sequence (one/modeling_one.py:338, 550-568): not built.
     * ``use_flash_attention=True`` replaces the feature-level softmax with causal attention
       across the call's tokens (one/modeling_one.py:408-421, TurboFlashAttention in
-      one/turbo_ops.py:437-475).
-    * ``use_single_token=True`` computes the attention of each sequence's last position only
-      and broadcasts it over the sequence (one/modeling_one.py:338, 550-568).
+      one/turbo_ops.py:437-475): built for bf16 models (the engine refuses other shapes).
     """
-    for flag in ("use_flash_attention", "use_single_token"):
-        if getattr(config, flag, False):
-            raise NotImplementedError(f"OneConfig.{flag}=True is not supported by the B200 engine")
+    if getattr(config, "use_single_token", False):
+        raise NotImplementedError("OneConfig.use_single_token=True is not supported by the B200 engine")
+    if getattr(config, "use_flash_attention", False) and dtype != torch.bfloat16:
+        raise NotImplementedError("OneConfig.use_flash_attention=True is built for bf16 models only")
 
 
 class OneEngine:
     def __init__(self, config, state_dict: Dict[str, torch.Tensor], device="cuda", dtype=torch.bfloat16,
                  max_batch: int = 256, max_tokens: Optional[int] = None, hist_cap: int = 4096,
                  max_positions: int = 8192):
-        check_supported(config)
+        check_supported(config, dtype)
         if not torch.cuda.is_available():
             raise C.OneError("OneEngine needs a CUDA device (B200, sm_100a)")
         self.cfg = config
@@ -102,7 +103,8 @@ class OneEngine:
             intermediate_size=config.intermediate_size, num_experts=config.num_experts if use_moe else 0,
             top_k=min(config.top_k_experts, config.num_experts) if use_moe else 0, r=config.r if use_moe else 0,
             mlp_bias=1 if config.mlp_bias else 0, dtype=C.dtype_code(dtype),
-            rms_norm_eps=config.rms_norm_eps, rope_theta=config.rope_theta)
+            rms_norm_eps=config.rms_norm_eps, rope_theta=config.rope_theta,
+            use_flash_attention=1 if getattr(config, "use_flash_attention", False) else 0)
 
         # ---- weights, packed to the engine's layout (device tensors owned here)
         self._keep = []

@@ -53,6 +53,8 @@ class OracleConfig:
     rope_theta: float = 10000.0
     hidden_act: str = "gelu"
     mlp_bias: bool = False
+    # use_flash_attention with the reference's turbo semantics (see flash_path_attention)
+    use_flash_attention: bool = False
 
     @property
     def use_moe(self) -> bool:
@@ -307,6 +309,28 @@ def feature_attention(single_x: Tensor, key: Tensor, value: Tensor, cos: Tensor,
     return w * v
 
 
+def flash_path_attention(single_x: Tensor, key: Tensor, value: Tensor, cos: Tensor, sin: Tensor,
+                         lq: Tuple[Tensor, Tensor], lk: Tuple[Tensor, Tensor], lv: Tuple[Tensor, Tensor]) -> Tensor:
+    """The model's use_flash_attention branch (one/modeling_one.py:408-421) under TURBO_MODE, where
+    ``self.flash_attention`` is ``TurboFlashAttention(causal=True)`` (:298-300,
+    one/turbo_ops.py:437-475), i.e. turbo_flash_attention's exact causal attention with the
+    default scale 1/sqrt(q.size(-1)) (one/turbo_ops.py:115-143) across the call's tokens.
+
+    single_x/key/value: [b, H, t, Dh] (single_x already scaled); returns [b, H, t, H].
+
+    Without TURBO_MODE the reference takes ``OneFlashAttention`` instead, whose call unpacks
+    ``flash_attention()``'s single tensor into two names (one/flash_attention.py:311): that
+    raises for a batch other than 2 and the layer falls back to the feature attention (:422-448),
+    and for a batch of 2 the unpacked 3-d result then fails in the rearrange (:550). The turbo
+    semantics are the only ones the flag has for every batch, and the engine follows them.
+    """
+    xr, kr = apply_rope(single_x, key, cos, sin)
+    q = F.linear(xr, *lq)
+    k = F.linear(kr, *lk)
+    v = F.linear(value, *lv)
+    return exact_attention(q, k, v, True)
+
+
 def exact_attention(q: Tensor, k: Tensor, v: Tensor, causal: bool, scale: Optional[float] = None) -> Tensor:
     """turbo_flash_attention's PyTorch path (one/turbo_ops.py:115-143): exact softmax
     attention in the input dtype with an fp32 softmax."""
@@ -435,7 +459,8 @@ def _moe(x: Tensor, p: Dict[str, Tensor], cfg: OracleConfig) -> Tensor:
 # --------------------------------------------------------------------------- one layer
 def one_layer(h: Tensor, hx: Tensor, cx: Tensor, lp: Dict[str, object], cos: Tensor, sin: Tensor,
               mean_fn, cfg: OracleConfig):
-    """One.forward (one/modeling_one.py:325-590) for use_flash_attention=False.
+    """One.forward (one/modeling_one.py:325-590); the attention is the feature attention, or with
+    ``cfg.use_flash_attention`` the causal attention across the call's tokens (:408-421).
 
     ``mean_fn(norm_x)`` returns the running mean ``hidden_state_sum`` (:358-387);
     the caller owns the history / running sum. Returns (output, hx, cx, norm_x).
@@ -448,7 +473,10 @@ def one_layer(h: Tensor, hx: Tensor, cx: Tensor, lp: Dict[str, object], cos: Ten
     single_x = F.linear(norm_x, *lp["lin1"]).view(b, s, H, Dh).permute(0, 2, 1, 3)    # :390,394-399
     key = F.linear(hx, *lp["lin2"]).view(b, s, H, Dh).permute(0, 2, 1, 3)             # :391,400-402
     single_x = single_x * (1.0 / math.sqrt(Dh))                                       # :405
-    o = feature_attention(single_x, key, value, cos, sin, lp["lin_q"], lp["lin_k"], lp["lin_v"])  # :515-547
+    if cfg.use_flash_attention:
+        o = flash_path_attention(single_x, key, value, cos, sin, lp["lin_q"], lp["lin_k"], lp["lin_v"])  # :408-421
+    else:
+        o = feature_attention(single_x, key, value, cos, sin, lp["lin_q"], lp["lin_k"], lp["lin_v"])  # :515-547
     o = o.permute(0, 2, 1, 3).reshape(b, s, H * H)                                    # :550-556
     hx_m = torch.clamp(_moe(o, lp["hx_moe"], cfg), min=-100, max=100)                 # :559
     x_m = torch.clamp(_moe(o, lp["x_moe"], cfg), min=-100, max=100)                   # :560

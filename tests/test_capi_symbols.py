@@ -35,4 +35,4 @@ def test_library_exports_every_declared_symbol():
 def test_binding_matches_header():
     from one import _capi
     assert set(_capi.SIGNATURES) == declared()
-    assert _capi.LIB.one_abi_version() == 1
+    assert _capi.LIB.one_abi_version() == _capi.ABI_VERSION == 2

@@ -32,17 +32,21 @@ def test_decode_divisors_fp32_are_positions():
     assert float(t[0]) == 1.0 and float(t[4097]) == 4097.0
 
 
-@pytest.mark.parametrize("flag", ["use_flash_attention", "use_single_token"])
-def test_unsupported_switches_raise(flag):
-    """The engine refuses the switches whose reference path it does not compute, before it
-    touches a device, instead of silently returning the default path's numbers."""
+@pytest.mark.parametrize("flag,dtype", [("use_single_token", torch.bfloat16), ("use_flash_attention", torch.float32)])
+def test_unsupported_switches_raise(flag, dtype):
+    """The engine refuses the switches whose reference path it does not compute (use_single_token;
+    use_flash_attention outside bf16), before it touches a device, instead of silently returning
+    the default path's numbers."""
     cfg = tiny_config()
     setattr(cfg, flag, True)
     with pytest.raises(NotImplementedError, match=flag):
-        check_supported(cfg)
+        check_supported(cfg, dtype)
     with pytest.raises(NotImplementedError, match=flag):
-        OneEngine(cfg, {}, "cpu", torch.bfloat16)
+        OneEngine(cfg, {}, "cpu", dtype)
 
 
 def test_default_switches_accepted():
     check_supported(tiny_config())
+    cfg = tiny_config()
+    cfg.use_flash_attention = True
+    check_supported(cfg, torch.bfloat16)

@@ -22,7 +22,8 @@ def ocfg(cfg):
     return O.OracleConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size, transformer_dim=cfg.transformer_dim,
                           num_hidden_layers=cfg.num_hidden_layers, num_attention_heads=cfg.num_attention_heads,
                           head_dim=cfg.head_dim, intermediate_size=cfg.intermediate_size, num_experts=cfg.num_experts,
-                          top_k_experts=cfg.top_k_experts, r=cfg.r)
+                          top_k_experts=cfg.top_k_experts, r=cfg.r,
+                          use_flash_attention=bool(getattr(cfg, "use_flash_attention", False)))
 
 
 def sd_for(dt):
