@@ -625,6 +625,98 @@ def run_prefill_reference(args):
     print(json.dumps(line), flush=True)
 
 
+C5_PROMPTS, C5_LEN, C5_CALL, C5_DECODE, C5_DEC_B = 4096, 4096, 64, 32768, 64
+C5_METRIC = "config 5: prompt ingestion tok/s (4096 prompts x 4096 tokens over the GPUs) and decode tok/s (batch 64)"
+
+
+def run_config5(args, ws, rank, local):
+    """The stated prompt-ingestion + long-decode workload at its full size: 4096 prompts of 4096
+    tokens (ids uniform, seed 5) split evenly over the GPUs and ingested 64 prompts per call,
+    then 32768 greedy decode steps of the last call's 64 sequences on every GPU (positions
+    4096 .. 36863), each step a CUDA-graph replay. Checks: the device error record stays clear,
+    and the last-position logits of two of the prompts match the oracle's forward over the
+    whole 4096-token prompt (bf16 tolerance 2e-2). The ingestion and the decode are each timed
+    with CUDA events, max over ranks."""
+    from one.configuration_one import config_140m
+    from one.engine import OneEngine
+    from one.initialization import init_state_dict
+    cfg = config_140m()
+    dev = f"cuda:{local}"
+    prompts = args.c5_prompts // ws
+    calls = max(1, prompts // C5_CALL)
+    dsteps = args.c5_steps
+    sd = init_state_dict(cfg, SEED, torch.bfloat16)
+    eng = OneEngine(cfg, sd, dev, torch.bfloat16, max_batch=C5_CALL, max_tokens=C5_CALL * C5_LEN,
+                    hist_cap=dsteps + 16, max_positions=C5_LEN + dsteps + 16)
+    g = torch.Generator().manual_seed(PF_SEED)
+    all_ids = torch.randint(0, cfg.vocab_size, (args.c5_prompts, C5_LEN), generator=g)
+    mine = all_ids[rank * prompts:(rank + 1) * prompts]
+    stream = torch.cuda.current_stream()
+    eng.prefill(mine[:C5_CALL, :64].to(dev))  # warm-up (kernel attributes, tables)
+    torch.cuda.synchronize()
+    barrier(ws)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        p0.record(stream)
+        for c in range(calls):
+            lg = eng.prefill(mine[c * C5_CALL:(c + 1) * C5_CALL].to(dev, non_blocking=True), logits="last")
+        p1.record(stream)
+        p1.synchronize()
+        pf_ms = max_over_ranks(ws, p0.elapsed_time(p1))
+        if eng.device_error() != (0, 0):
+            raise RuntimeError(f"device error after prompt ingestion {eng.device_error()}")
+        # the last call's prompts 0 and 63 against the oracle over the whole prompt
+        checked = 0
+        if rank == 0:
+            from oracle import one_oracle as O
+            oc = O.OracleConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
+                                transformer_dim=cfg.transformer_dim, num_hidden_layers=cfg.num_hidden_layers,
+                                num_attention_heads=cfg.num_attention_heads, head_dim=cfg.head_dim,
+                                intermediate_size=cfg.intermediate_size, num_experts=cfg.num_experts,
+                                top_k_experts=cfg.top_k_experts, r=cfg.r)
+            last = mine[(calls - 1) * C5_CALL:calls * C5_CALL]
+            rows = [0, C5_CALL - 1]
+            torch.set_num_threads(os.cpu_count() or 1)
+            with torch.no_grad():
+                ref = O.forward(sd, last[rows], oc, torch.bfloat16, last_only=True).logits[:, -1].float()
+            got = lg.view(C5_CALL, -1)[rows].float().cpu()
+            bad = (got - ref).abs() > 2e-2 + 2e-2 * ref.abs()
+            if bool(bad.any()):
+                raise RuntimeError(f"last-position logits differ from the oracle at {int(bad.sum())} entries")
+            checked = len(rows)
+        # decode: 32768 steps of the last call's sequences
+        eng.capture(1)
+        eng.replay()
+        torch.cuda.synchronize()
+        barrier(ws)
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for _ in range(dsteps - 1):
+            eng.replay()
+        d1.record(stream)
+        d1.synchronize()
+        dec_ms = max_over_ranks(ws, d0.elapsed_time(d1))
+    if eng.device_error() != (0, 0):
+        raise RuntimeError(f"device error after decode {eng.device_error()}")
+    hist = eng.history(dsteps, C5_CALL)
+    assert int(hist.min()) >= 0 and int(hist.max()) < cfg.vocab_size
+    if rank == 0:
+        tokens = ws * calls * C5_CALL * C5_LEN
+        line = {"metric": C5_METRIC, "value": tokens / (pf_ms / 1000.0), "unit": "tok/s", "n_gpus": ws,
+                "steps": calls, "warmup": 1, "ms_per_step": pf_ms / calls, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init weights N(0,0.02) seed 4, prompt ids uniform seed 5)",
+                "config": {"workload": f"140M-class One bf16: {ws * calls * C5_CALL} prompts x {C5_LEN} tokens "
+                                       f"({calls} calls of {C5_CALL} per GPU), then {dsteps} decode steps at batch "
+                                       f"{C5_CALL} per GPU (positions {C5_LEN} .. {C5_LEN + dsteps - 1})",
+                           "prefill_s": pf_ms / 1000.0, "decode_steps": dsteps,
+                           "decode_ms_per_step": dec_ms / (dsteps - 1),
+                           "decode_tok_s": ws * C5_CALL * (dsteps - 1) / (dec_ms / 1000.0),
+                           "oracle_checked_prompts": checked},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+
+
 MOE_T, MOE_D, MOE_E, MOE_K, MOE_R = 16384, 768, 8, 2, 64
 MOE_METRIC = "LinearMoE TFLOP/s (16384 x 768 bf16, 8 experts top-2, r 64, 768 -> 768)"
 
@@ -801,9 +893,12 @@ def main():
                     help="decode: fixed global batch split over the GPUs (strong scaling); default 256 per GPU")
     ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
     ap.add_argument("--profile-prefill", action="store_true", help="run the small prompt-ingestion ncu case and exit")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe", "prefill", "config5"],
                     help="decode: the 140M decode step (default); attention: the isolated RoPE + attention op; "
-                         "linear_moe: the isolated LinearMoE op on 16384 tokens; prefill: 64 x 4096-token prompts")
+                         "linear_moe: the isolated LinearMoE op on 16384 tokens; prefill: 64 x 4096-token prompts; "
+                         "config5: 4096 x 4096 prompts over the GPUs, then 32768 decode steps at batch 64")
+    ap.add_argument("--c5-prompts", type=int, default=C5_PROMPTS, help="config5: prompts over all GPUs")
+    ap.add_argument("--c5-steps", type=int, default=C5_DECODE, help="config5: decode steps")
     args = ap.parse_args()
     if args.profile_prefill:
         profile_prefill(args)
@@ -831,6 +926,8 @@ def main():
             run_linear_moe(args, ws, rank, local)
         elif args.workload == "prefill":
             run_prefill(args, ws, rank, local)
+        elif args.workload == "config5":
+            run_config5(args, ws, rank, local)
         else:
             run_native(args, ws, rank, local)
     finally:

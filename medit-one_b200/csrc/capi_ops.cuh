@@ -9,6 +9,19 @@ __global__ void clamp_copy_kernel(const T* x, T* y, long n, float lim) {
   if (i < n) st<T>(y + i, fminf(fmaxf(ld<T>(x + i), -lim), lim));
 }
 
+// x.clamp(-1e4, 1e4) of a bf16 tensor (one/linear_moe.py:53), 16 bytes per thread per
+// iteration over a grid of a few CTAs per SM: the bound is bf16(1e4) = 9984, and each packed
+// min / max is exact, so the values equal clamp_copy_kernel's. n8 = elements / 8.
+__global__ void clamp_copy_bf16x8_kernel(const uint4* x, uint4* y, long n8) {
+  pdl_wait();
+  const uint32_t hi = 0x461c461cu, lo = 0xc61cc61cu;  // +-9984
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    const uint4 v = x[i];
+    y[i] = make_uint4(bf2_min(bf2_max(v.x, lo), hi), bf2_min(bf2_max(v.y, lo), hi), bf2_min(bf2_max(v.z, lo), hi),
+                      bf2_min(bf2_max(v.w, lo), hi));
+  }
+}
+
 static size_t align1k(size_t x) { return (x + 1023) & ~size_t(1023); }
 
 extern "C" size_t one_linear_moe_workspace_bytes(int32_t n, int32_t fin, int32_t r, int32_t dtype) {
@@ -41,11 +54,18 @@ extern "C" int one_linear_moe(const void* x, int32_t n, int32_t fin, int32_t fou
   void* glog = ws + 2 * align1k((size_t)n * fin * es);
   // x.clamp(-1e4, 1e4) (one/linear_moe.py:53)
   const long total = (long)n * fin;
-  cudaError_t ce = dtype == ONE_DTYPE_BF16
-                       ? launch_k(clamp_copy_kernel<__nv_bfloat16>, dim3((total + 255) / 256), dim3(256), 0, st,
-                                  (const __nv_bfloat16*)x, (__nv_bfloat16*)xc, total, 1e4f)
-                       : launch_k(clamp_copy_kernel<float>, dim3((total + 255) / 256), dim3(256), 0, st, (const float*)x,
-                                  (float*)xc, total, 1e4f);
+  cudaError_t ce;
+  if (dtype == ONE_DTYPE_BF16 && total % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const long n8 = total / 8;
+    const long blocks = std::min<long>((n8 + 255) / 256, (long)num_sms() * 8);
+    ce = launch_k(clamp_copy_bf16x8_kernel, dim3((unsigned)blocks), dim3(256), 0, st, (const uint4*)x, (uint4*)xc, n8);
+  } else {
+    ce = dtype == ONE_DTYPE_BF16
+             ? launch_k(clamp_copy_kernel<__nv_bfloat16>, dim3((total + 255) / 256), dim3(256), 0, st,
+                        (const __nv_bfloat16*)x, (__nv_bfloat16*)xc, total, 1e4f)
+             : launch_k(clamp_copy_kernel<float>, dim3((total + 255) / 256), dim3(256), 0, st, (const float*)x,
+                        (float*)xc, total, 1e4f);
+  }
   if (ce != cudaSuccess) return fail(ONE_ERR_CUDA, "clamp launch: %s", cudaGetErrorString(ce));
   // gate logits (:56)
   Launch g;
