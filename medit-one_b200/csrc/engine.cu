@@ -203,8 +203,8 @@ static int num_sms() {
 // Token-tile width: enough CTAs to cover the SMs twice where possible, wider tiles
 // (fewer weight re-reads from L2) when the problem already has many weight tiles.
 static int pick_bn(int T, int m_tiles_total) {
-  if (T >= 8192 && m_tiles_total * ((T + 255) / 256) >= num_sms()) return 256;
-  if (T >= 2048 && m_tiles_total * ((T + 127) / 128) >= num_sms()) return 128;
+  if (T >= 8192) return 256;
+  if (T >= 2048) return 128;
   for (int bn : {256, 128, 64}) {
     const int ctas = m_tiles_total * ((T + bn - 1) / bn);
     if (bn <= T * 2 && ctas >= num_sms()) return bn;
