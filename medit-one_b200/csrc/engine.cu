@@ -114,6 +114,9 @@ struct ProbSpec {
   int lda = 0;
   float* ws = nullptr;
   int ldw = 0;
+  // (first problem's) decode GEMM followed by the attention/router kernel: 64-token tiles with a
+  // deep ring on at most one CTA per SM, leaving SMs free for that kernel's prologue
+  bool leave_sms = false;
   unsigned long long* best = nullptr;
   int max_splits = 1;
 };
@@ -161,6 +164,7 @@ __global__ void next_ids_kernel(const NextIdsParams p) {
 struct Launch {
   LaunchKind kind;
   int bn = 0;       // tensor-core tile width
+  int stages = 0;   // ring depth of gemm_bf16_tc_kernel (0: the default for bn)
   int persist = 0;  // gemm_bf16_tc_persistent (one CTA per SM looping over the tiles)
   int minb = 1;  // row_attn: CTAs per SM the instantiation is compiled for
   int grid = 1, block = 1;
@@ -215,6 +219,18 @@ static int pick_bn(int T, int m_tiles_total) {
   return T > 32 ? 64 : 32;
 }
 
+// Ring depth of the deep per-tile GEMM instantiations (one CTA per SM).
+constexpr int kDeepStages = 6;
+static int tc_smem(int BN, int stages) {
+  if (stages == kDeepStages && BN == 64) return TcCfg<64, kDeepStages>::kSmem;
+  switch (BN) {
+    case 32: return TcCfg<32>::kSmem;
+    case 64: return TcCfg<64>::kSmem;
+    case 128: return TcCfg<128>::kSmem;
+    default: return TcCfg<256>::kSmem;
+  }
+}
+
 // Build one GEMM launch over up to four independent problems sharing T tokens.
 static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, DevErr* err) {
   if (n < 1 || n > kMaxProblems) return fail(ONE_ERR_INVALID, "bad problem count");
@@ -233,7 +249,16 @@ static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, Dev
   }
   int mt_total = 0;
   for (int i = 0; i < n; ++i) mt_total += (ps[i].Nw + 127) / 128;
-  const int BN = tc ? pick_bn(T, mt_total) : 64;
+  int BN = tc ? pick_bn(T, mt_total) : 64;
+  bool deep = false;
+  if (tc && ps[0].leave_sms && T <= 256 && mt_total * ((T + 63) / 64) <= num_sms()) {
+    int kb = 0;
+    for (int i = 0; i < n; ++i) kb = std::max(kb, (ps[i].K + 63) / 64);
+    if (kb >= kDeepStages) {
+      BN = 64;
+      deep = true;
+    }
+  }
   const int BM = tc ? 128 : 64;
   L.kind = tc ? L_GEMM_TC : L_GEMM_SIMT;
   L.bn = BN;
@@ -297,12 +322,8 @@ static int plan_gemm(Launch& L, const ProbSpec* ps, int n, int T, int dtype, Dev
       L.grid = num_sms();
       return ONE_OK;
     }
-    switch (BN) {
-      case 32: L.smem = TcCfg<32>::kSmem; break;
-      case 64: L.smem = TcCfg<64>::kSmem; break;
-      case 128: L.smem = TcCfg<128>::kSmem; break;
-      default: L.smem = TcCfg<256>::kSmem; break;
-    }
+    L.stages = deep ? kDeepStages : 0;
+    L.smem = tc_smem(BN, L.stages);
   } else {
     L.sg.nprob = n;
     L.sg.total_tiles = tiles;
@@ -338,6 +359,8 @@ static bool g_attrs_set = false;
 static int set_kernel_attrs() {
   if (g_attrs_set) return ONE_OK;
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<32>::kSmem));
+  CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<64, kDeepStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          TcCfg<64, kDeepStages>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<64>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<128>::kSmem));
   CK(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::kSmem));
@@ -426,10 +449,13 @@ static int run(const Launch& L, cudaStream_t st) {
         e = launch_k(gemm_bf16_tc_persistent, dim3(L.grid), dim3(L.block), L.smem, st, L.g);
         break;
       }
-      switch (L.bn) {
-        case 32: e = launch_k(gemm_bf16_tc_kernel<32>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
-        case 64: e = launch_k(gemm_bf16_tc_kernel<64>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
-        case 128: e = launch_k(gemm_bf16_tc_kernel<128>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
+      switch (L.bn * 100 + L.stages) {
+        case 3200: e = launch_k(gemm_bf16_tc_kernel<32>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
+        case 6400: e = launch_k(gemm_bf16_tc_kernel<64>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
+        case 12800: e = launch_k(gemm_bf16_tc_kernel<128>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
+        case 6400 + kDeepStages:
+          e = launch_k(gemm_bf16_tc_kernel<64, kDeepStages>, dim3(L.grid), dim3(L.block), L.smem, st, L.g);
+          break;
         default: e = launch_k(gemm_bf16_tc_kernel<256>, dim3(L.grid), dim3(L.block), L.smem, st, L.g); break;
       }
       break;
@@ -924,6 +950,7 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
         ps[n].W = LW(ONE_W_CX_GATE); ps[n].Nw = c.r; ps[n].K = D; ps[n].X = B_(e->b.cxc[cur]); ps[n].ldx = D;
         ps[n].bias = nullptr; ps[n].out = B_(e->b.gcx); ps[n].ldo = c.r; ++n;
       }
+      ps[0].leave_sms = decode && dec_attn_eligible(c);
       Launch g;
       int rc = plan_gemm(g, ps, n, T, dt, err);
       if (rc) return rc;

@@ -139,10 +139,12 @@ ONE_DEVINL void epi_gelu_pair(const GemmProblem& P, int n_even, int t, float g, 
 
 
 // ------------------------------------------------------------------ tensor-core kernel
-template <int BN>
+// ST > 0: a deeper ring (more bytes in flight per CTA, one CTA per SM) for launches whose
+// CTAs each have an SM to themselves.
+template <int BN, int ST = 0>
 struct TcCfg {
-  // pipeline depth that keeps two CTAs per SM (<= ~100 KB of stages)
-  static constexpr int kStages = BN >= 256 ? 2 : (BN >= 128 ? 3 : 4);
+  // default pipeline depth: keeps two CTAs per SM (<= ~100 KB of stages)
+  static constexpr int kStages = ST > 0 ? ST : (BN >= 256 ? 2 : (BN >= 128 ? 3 : 4));
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = BN * 64 * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -394,9 +396,9 @@ ONE_DEVINL void gemm_tile_coords(const GemmParams& p, int tile, int& pi, int& m_
   nkb = min(kb0 + P.kb_per_split, kb_total) - kb0;
 }
 
-template <int BN>
+template <int BN, int ST = 0>
 __global__ void __launch_bounds__(192, 2) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
-  using C = TcCfg<BN>;
+  using C = TcCfg<BN, ST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
