@@ -217,10 +217,24 @@ def cpu_reference(cfg, steps: int, warmup: int, batch: int, contexts=CPU_CONTEXT
         del dec
     w = CPU_WEIGHTS if len(contexts) == 3 else tuple(1.0 / len(contexts) for _ in contexts)
     mean_step = sum(wi * ti for wi, ti in zip(w, per_step))
+    # the same ops with the O(1) running sum in place of the history cumsum (the engine's
+    # algorithm on the CPU): context-independent
+    run = O.RunningDecoder(sd, oc, torch.bfloat16)
+    g = torch.Generator().manual_seed(SEED)
+    run.S = [torch.randn(batch, cfg.transformer_dim, generator=g) for _ in range(cfg.num_hidden_layers)]
+    run.P = contexts[0]
+    ids = torch.randint(0, cfg.vocab_size, (batch, 1), generator=g)
+    with torch.no_grad():
+        ids = run.step(ids).logits[:, -1].argmax(-1, keepdim=True)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            ids = run.step(ids).logits[:, -1].argmax(-1, keepdim=True)
+        o1 = (time.perf_counter() - t0) / steps
     return {"value": batch / mean_step, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{steps} decode steps of {batch} sequences at each context {list(contexts)} "
                       f"({warmup} untimed each; step s {[round(t, 3) for t in per_step]}), Simpson-weighted over the "
                       f"{DECODE_STEPS}-step run; oracle restatement of the reference's cached decode, bf16",
+            "o1_tok_s": batch / o1,
             "seconds": total, "step_seconds": per_step, "contexts": list(contexts)}
 
 
@@ -240,7 +254,7 @@ def run_reference(args, ws, rank):
             "config": {"workload": f"140M-class One, bf16, greedy decode of 256 sequences, {DECODE_STEPS} steps after a "
                                    f"{PROMPT}-token prompt (step time sampled at contexts {list(CPU_CONTEXTS)})",
                        "batch": BATCH, "prompt": PROMPT},
-            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "o1_tok_s")},
             "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -369,7 +383,7 @@ def run_native(args, ws, rank, local):
         }
         if ws == 1 and not args.no_cpu_baseline:
             r = cpu_reference(cfg, 2, 1, BATCH)
-            line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "o1_tok_s")}
         print(json.dumps(line), flush=True)
 
 
