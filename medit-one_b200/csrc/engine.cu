@@ -1273,7 +1273,7 @@ static int build_final(one_engine* e, std::vector<Launch>& plan, int T, int batc
     q.err = err;
     g.block = LmCfg::kThreads;
     g.smem = LmCfg::kSmem;
-    g.grid = ((c.vocab_size + kLmBN - 1) / kLmBN) * q.t_tiles;
+    g.grid = ((c.vocab_size + kLmBN - 1) / kLmBN) * ((q.t_tiles + kLmTT - 1) / kLmTT);
     plan.push_back(g);
   } else {
     ProbSpec ps[1];

@@ -841,16 +841,19 @@ namespace one {
 // Tokens are the UMMA A operand (M = 128 token rows per tile) and a 256-row vocabulary tile is
 // B (N = 256), so TMEM lane i holds token i's 256 logits of the tile: each epilogue thread scans
 // its own row in vocabulary order and needs no cross-thread reduction. One CTA per (vocabulary
-// tile, token tile); the two token tiles of a vocabulary tile are adjacent CTAs, so the tile is
-// read from HBM once and from L2 the second time. Warp 0 streams both operands through a
-// kLmStages ring (weight tiles of the first stages before the dependency wait), warp 1 issues
-// the MMAs, warps 2..5 scan the accumulator.
-constexpr int kLmStages = 4;
+// tile, pair of token tiles): both token tiles of a decode step (256 tokens) multiply the same
+// vocabulary tile into two TMEM accumulators, so the 125 vocabulary tiles of a 32000-word head
+// run as one wave of 125 CTAs (a CTA per token tile made 250 CTAs of one per SM: two waves).
+// Lane 0 of warps 2..2+S-1 streams both operands of one ring slot each (the vocabulary tiles of
+// the first stages before the dependency wait), warp 1 issues the MMAs, warps 2..5 scan the
+// accumulators.
+constexpr int kLmStages = 3;
 constexpr int kLmBN = 256;  // vocabulary rows per tile
+constexpr int kLmTT = 2;    // token tiles per CTA
 struct LmCfg {
-  static constexpr int kABytes = 128 * 64 * 2;    // token tile
+  static constexpr int kABytes = 128 * 64 * 2;    // one token tile
   static constexpr int kBBytes = kLmBN * 64 * 2;  // vocabulary tile
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStageBytes = kLmTT * kABytes + kBBytes;
   static constexpr int kSmem = kLmStages * kStageBytes + 1024 + 256;
   static constexpr int kThreads = 192;
 };
@@ -875,7 +878,9 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
   uint64_t* accb = empty + kLmStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int v_tile = blockIdx.x / p.t_tiles, t_tile = blockIdx.x % p.t_tiles;
+  const int t_pairs = (p.t_tiles + kLmTT - 1) / kLmTT;
+  const int v_tile = blockIdx.x / t_pairs, tt0 = (blockIdx.x % t_pairs) * kLmTT;
+  const int ntt = min(kLmTT, p.t_tiles - tt0);  // token tiles of this CTA
   const int nkb = (p.K + 63) / 64;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kLmStages; ++s) {
@@ -886,7 +891,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kLmBN);
+    tmem_alloc(tmem_slot, kLmTT * kLmBN);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
@@ -898,8 +903,8 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) pdl_launch_dependents();
-  auto sA = [&](int s) { return smem + s * LmCfg::kStageBytes; };
-  auto sB = [&](int s) { return smem + s * LmCfg::kStageBytes + LmCfg::kABytes; };
+  auto sA = [&](int s, int tt) { return smem + s * LmCfg::kStageBytes + tt * LmCfg::kABytes; };
+  auto sB = [&](int s) { return smem + s * LmCfg::kStageBytes + kLmTT * LmCfg::kABytes; };
 
   if (warp >= 2 && warp < 2 + kLmStages) {
     // TMA issue, one thread per slot: one thread's bulk copies complete one after another
@@ -921,8 +926,8 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
           mbar_arrive_expect_tx(&full[slot], LmCfg::kBBytes);
           tma_load_2d_hint(sB(slot), &p.tmw, &full[slot], i * 64, v_tile * kLmBN, wpol);
         }
-        mbar_arrive_expect_tx(&full[slot], LmCfg::kABytes);
-        tma_load_2d(sA(slot), &p.tmx, &full[slot], i * 64, t_tile * 128);
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)ntt * LmCfg::kABytes);
+        for (int tt = 0; tt < ntt; ++tt) tma_load_2d(sA(slot, tt), &p.tmx, &full[slot], i * 64, (tt0 + tt) * 128);
       }
     }
     __syncwarp();
@@ -935,29 +940,33 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
         const uint32_t ph = (uint32_t)(i / kLmStages) & 1u;
         if (!mbar_wait(&full[s], ph, p.err, 42)) break;
         tc_fence_after();
-        const uint64_t ad = umma_desc_sw128(sA(s));
         const uint64_t bd = umma_desc_sw128(sB(s));
+        for (int tt = 0; tt < ntt; ++tt) {
+          const uint64_t ad = umma_desc_sw128(sA(s, tt));
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + (uint32_t)(tt * kLmBN), ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(accb);
     }
   } else if (warp >= 2) {
-    // ---- epilogue: warp w scans TMEM lanes 32 (w % 4) .. +31 = its 32 tokens
+    // ---- epilogue: warp w scans TMEM lanes 32 (w % 4) .. +31 = its 32 tokens of each tile
     pdl_wait();
     const int q = warp & 3;
-    const int t = t_tile * 128 + q * 32 + lane;
     const bool ok = mbar_wait(accb, 0, p.err, 43);
     tc_fence_after();
+    const int v0 = v_tile * kLmBN;
+    for (int tt = 0; tt < ntt; ++tt) {
+    const int t = (tt0 + tt) * 128 + q * 32 + lane;
     uint32_t best16 = 0u;  // order-preserving bf16 bits of the best rounded logit (0: none)
     int best_v = 0;
-    const int v0 = v_tile * kLmBN;
     if (ok) {
       for (int c0 = 0; c0 < kLmBN; c0 += 32) {
         if (v0 + c0 >= p.V) break;  // warp-uniform
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tt * kLmBN + c0), v);
         tmem_ld_wait();
         uint32_t h[16];
 #pragma unroll
@@ -988,13 +997,14 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
     }
     if (ok && t < p.T && best16)
       atomicMax(p.best + t, ((unsigned long long)best16 << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)best_v));
+    }
   }
   __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kLmBN);
+    tmem_dealloc(tmem, kLmTT * kLmBN);
   }
 }
 
