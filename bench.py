@@ -917,6 +917,26 @@ def profile_prefill(args):
     print(json.dumps({"profile_prefill": "ok", "tokens": b * s, "launches": eng.prefill_launches(b, s)}))
 
 
+def profile_flash(args):
+    """Small fixed case for ncu captures of the use_flash_attention path: the 140M model with the
+    flag set, one prompt-ingestion call of 4 prompts x 2048 tokens (launch order per layer: row_pre,
+    scan, GEMM A, q | k | v per token, the causal sequence attention, ...)."""
+    from one.configuration_one import config_140m
+    from one.engine import OneEngine
+    from one.initialization import init_state_dict
+    cfg = config_140m()
+    cfg.use_flash_attention = True
+    b, s = 4, 2048
+    eng = OneEngine(cfg, init_state_dict(cfg, SEED, torch.bfloat16), "cuda", torch.bfloat16, max_batch=b,
+                    max_tokens=b * s)
+    g = torch.Generator().manual_seed(PF_SEED)
+    eng.prefill(torch.randint(0, cfg.vocab_size, (b, s), generator=g).cuda())
+    torch.cuda.synchronize()
+    if eng.device_error() != (0, 0):
+        raise RuntimeError(f"device error {eng.device_error()}")
+    print(json.dumps({"profile_flash": "ok", "tokens": b * s, "launches": eng.prefill_launches(b, s)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -928,6 +948,8 @@ def main():
                     help="decode: fixed global batch split over the GPUs (strong scaling); default 256 per GPU")
     ap.add_argument("--profile-case", action="store_true", help="run the small ncu case and exit")
     ap.add_argument("--profile-prefill", action="store_true", help="run the small prompt-ingestion ncu case and exit")
+    ap.add_argument("--profile-flash", action="store_true",
+                    help="run the small use_flash_attention prompt-ingestion ncu case and exit")
     ap.add_argument("--workload", default="decode", choices=["decode", "attention", "linear_moe", "prefill", "config5"],
                     help="decode: the 140M decode step (default); attention: the isolated RoPE + attention op; "
                          "linear_moe: the isolated LinearMoE op on 16384 tokens; prefill: 64 x 4096-token prompts; "
@@ -937,6 +959,9 @@ def main():
     args = ap.parse_args()
     if args.profile_prefill:
         profile_prefill(args)
+        return
+    if args.profile_flash:
+        profile_flash(args)
         return
     if args.profile_case:
         profile_case(args)

@@ -496,7 +496,7 @@ static int run(const Launch& L, cudaStream_t st) {
       }
       break;
     case L_SEQ_ATTN:
-      e = launch_k(seq_attn_kernel, dim3(L.grid, L.sa.H, L.nv), dim3(kSeqQ), 0, st, L.sa);
+      e = launch_k(seq_attn_kernel, dim3(L.grid, L.sa.H, L.nv), dim3(kSeqThreads), 0, st, L.sa);
       break;
     case L_ROUTER:
       if (L.ro.np > 0) {
@@ -1047,7 +1047,7 @@ static int build_layers(one_engine* e, std::vector<Launch>& plan, int T, bool de
         sq.dtype = dt;
         sq.grid = (seq_len + kSeqQ - 1) / kSeqQ;
         sq.nv = batch;
-        sq.block = kSeqQ;
+        sq.block = kSeqThreads;
         sq.sa = SeqAttnParams{e->at<__nv_bfloat16>(e->b.proj), 3 * HD, e->at<__nv_bfloat16>(e->b.o), seq_len, H,
                               1.0f / sqrtf((float)H), moe ? 9984.0f : 0.0f};
         plan.push_back(sq);
