@@ -844,18 +844,23 @@ namespace one {
 // tile, pair of token tiles): both token tiles of a decode step (256 tokens) multiply the same
 // vocabulary tile into two TMEM accumulators, so the 125 vocabulary tiles of a 32000-word head
 // run as one wave of 125 CTAs (a CTA per token tile made 250 CTAs of one per SM: two waves).
-// Lane 0 of warps 2..2+S-1 streams both operands of one ring slot each (the vocabulary tiles of
-// the first stages before the dependency wait), warp 1 issues the MMAs, warps 2..5 scan the
-// accumulators.
+// One thread's bulk copies complete one after another (~0.4 us each on B200), so every copy of
+// a ring slot has its own issuing thread: lane 0 of warp 2 + 3 s streams slot s's vocabulary
+// tiles (the first before the dependency wait), lanes 0 of warps 3 + 3 s and 4 + 3 s its two
+// token tiles. Warp 1 issues the MMAs; warps 2..9 scan the accumulators, one token tile per
+// warp and 32 of its tokens (TMEM lane quarter warp % 4).
 constexpr int kLmStages = 3;
 constexpr int kLmBN = 256;  // vocabulary rows per tile
 constexpr int kLmTT = 2;    // token tiles per CTA
+constexpr int kLmCopies = 1 + kLmTT;  // bulk copies per ring slot
 struct LmCfg {
   static constexpr int kABytes = 128 * 64 * 2;    // one token tile
   static constexpr int kBBytes = kLmBN * 64 * 2;  // vocabulary tile
   static constexpr int kStageBytes = kLmTT * kABytes + kBBytes;
   static constexpr int kSmem = kLmStages * kStageBytes + 1024 + 256;
-  static constexpr int kThreads = 192;
+  static constexpr int kIssueWarps = kLmStages * kLmCopies;
+  static constexpr int kScanWarps = 4 * kLmTT;
+  static constexpr int kThreads = 32 * (2 + (kIssueWarps > kScanWarps ? kIssueWarps : kScanWarps));
 };
 static_assert(LmCfg::kSmem <= 227 * 1024, "lm_head shared memory");
 
@@ -884,7 +889,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
   const int nkb = (p.K + 63) / 64;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kLmStages; ++s) {
-      mbar_init(&full[s], 2);  // the weight copy and the token copy of the slot arrive
+      mbar_init(&full[s], 1 + ntt);  // the weight copy and each token-tile copy of the slot arrive
       mbar_init(&empty[s], 1);
     }
     mbar_init(accb, 1);
@@ -906,28 +911,30 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
   auto sA = [&](int s, int tt) { return smem + s * LmCfg::kStageBytes + tt * LmCfg::kABytes; };
   auto sB = [&](int s) { return smem + s * LmCfg::kStageBytes + kLmTT * LmCfg::kABytes; };
 
-  if (warp >= 2 && warp < 2 + kLmStages) {
-    // TMA issue, one thread per slot: one thread's bulk copies complete one after another
-    // (~0.4 us each on B200), so lane 0 of warp 2 + j loads both operands of the k blocks j,
-    // j + S, ... (S = kLmStages) before the warp turns to the epilogue. Weight tiles are not
-    // written by earlier kernels: each slot's first one is requested before the dependency wait.
+  if (warp >= 2 && warp < 2 + LmCfg::kIssueWarps) {
+    // TMA issue, one thread per copy of a slot, for the k blocks slot, slot + S, ...
+    // (S = kLmStages), before the warp turns to the epilogue
     if (lane == 0) {
-      const int slot = warp - 2;
-      const uint64_t wpol = l2_policy_evict_first();
-      if (slot < nkb) {
-        mbar_arrive_expect_tx(&full[slot], LmCfg::kBBytes);
-        tma_load_2d_hint(sB(slot), &p.tmw, &full[slot], slot * 64, v_tile * kLmBN, wpol);
-      }
-      pdl_wait();
-      for (int i = slot; i < nkb; i += kLmStages) {
-        const uint32_t ph = (uint32_t)(i / kLmStages) & 1u;
-        if (i >= kLmStages) {
-          if (!mbar_wait(&empty[slot], ph ^ 1u, p.err, 41)) break;
+      const int slot = (warp - 2) / kLmCopies, cp = (warp - 2) % kLmCopies;
+      if (cp == 0) {
+        // vocabulary tiles: never written by earlier kernels, so no dependency wait
+        const uint64_t wpol = l2_policy_evict_first();
+        for (int i = slot; i < nkb; i += kLmStages) {
+          const uint32_t ph = (uint32_t)(i / kLmStages) & 1u;
+          if (i >= kLmStages && !mbar_wait(&empty[slot], ph ^ 1u, p.err, 41)) break;
           mbar_arrive_expect_tx(&full[slot], LmCfg::kBBytes);
           tma_load_2d_hint(sB(slot), &p.tmw, &full[slot], i * 64, v_tile * kLmBN, wpol);
         }
-        mbar_arrive_expect_tx(&full[slot], (uint32_t)ntt * LmCfg::kABytes);
-        for (int tt = 0; tt < ntt; ++tt) tma_load_2d(sA(slot, tt), &p.tmx, &full[slot], i * 64, (tt0 + tt) * 128);
+      } else if (cp - 1 < ntt) {
+        // token tile cp - 1: the activations the previous kernel wrote
+        const int tt = cp - 1;
+        pdl_wait();
+        for (int i = slot; i < nkb; i += kLmStages) {
+          const uint32_t ph = (uint32_t)(i / kLmStages) & 1u;
+          if (i >= kLmStages && !mbar_wait(&empty[slot], ph ^ 1u, p.err, 44)) break;
+          mbar_arrive_expect_tx(&full[slot], LmCfg::kABytes);
+          tma_load_2d(sA(slot, tt), &p.tmx, &full[slot], i * 64, (tt0 + tt) * 128);
+        }
       }
     }
     __syncwarp();
@@ -951,14 +958,16 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
       }
       umma_commit(accb);
     }
-  } else if (warp >= 2) {
-    // ---- epilogue: warp w scans TMEM lanes 32 (w % 4) .. +31 = its 32 tokens of each tile
+  } else if (warp >= 2 && warp < 2 + LmCfg::kScanWarps && (warp - 2) / 4 < ntt) {
+    // ---- epilogue: warp w scans token tile (w - 2) / 4, TMEM lanes 32 (w % 4) .. +31 = its
+    // 32 tokens of that tile
     pdl_wait();
     const int q = warp & 3;
     const bool ok = mbar_wait(accb, 0, p.err, 43);
     tc_fence_after();
     const int v0 = v_tile * kLmBN;
-    for (int tt = 0; tt < ntt; ++tt) {
+    {
+    const int tt = (warp - 2) / 4;
     const int t = (tt0 + tt) * 128 + q * 32 + lane;
     uint32_t best16 = 0u;  // order-preserving bf16 bits of the best rounded logit (0: none)
     int best_v = 0;
