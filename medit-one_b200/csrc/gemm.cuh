@@ -232,6 +232,8 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
     load8(reinterpret_cast<const T*>(P.bias) + ng + 8, bg + 8);
   }
   uint4 auxr[KU];
+#pragma unroll
+  for (int k = 0; k < KU; ++k) auxr[k] = make_uint4(0, 0, 0, 0);
   auto aux_load = [&](int cc) {
 #pragma unroll
     for (int k = 0; k < KU; ++k) {
@@ -241,11 +243,13 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
         auxr[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.aux) + (size_t)t * P.lda + n0);
     }
   };
-  aux_load(0);
   // Two passes over the same code. Pass 0 runs on warps 2..5 while the MMAs are still in flight,
   // with the TMEM reads and every global store switched off: it only brings this code into the
   // instruction cache, where a cold epilogue otherwise spent about a microsecond missing after
-  // the accumulator was ready. Pass 1 is the epilogue proper, on all six warps.
+  // the accumulator was ready. Pass 1 is the epilogue proper, on all six warps. The first
+  // chunk's activation vectors are requested at the start of pass 1, before the accumulator
+  // wait: requested before pass 0, they held pass 0 (which computes on them) for a global-load
+  // latency, and the warps then met a ready accumulator late (0.6-1 us on the hx and x_moe GEMMs).
   bool ok = true;
 #pragma unroll 1
   for (int pass = drain ? 0 : 1; pass < 2; ++pass) {
@@ -253,6 +257,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmParams& p, const GemmProbl
   const int nt = dry ? 128 : NT;  // threads of the pass's named barrier
   const int bar = dry ? 2 : 1;    // its own barrier: warps 0 and 1 may already wait on barrier 1
   if (!dry) {
+    aux_load(0);
     ok = mbar_wait(accb, 0, p.err, 3);
     tc_fence_after();
   }
