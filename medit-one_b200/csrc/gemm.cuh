@@ -843,20 +843,23 @@ namespace one {
 // v of the rounded logits, torch.argmax) reduced into best[t] as an order-preserving 64-bit key
 // by atomicMax (argmax_key). Written only on request: the logits themselves.
 //
-// Tokens are the UMMA A operand (M = 128 token rows per tile) and a 256-row vocabulary tile is
-// B (N = 256), so TMEM lane i holds token i's 256 logits of the tile: each epilogue thread scans
+// Tokens are the UMMA A operand (M = 128 token rows per tile) and a 224-row vocabulary tile is
+// B (N = 224), so TMEM lane i holds token i's 224 logits of the tile: each epilogue thread scans
 // its own row in vocabulary order and needs no cross-thread reduction. One CTA per (vocabulary
 // tile, pair of token tiles): both token tiles of a decode step (256 tokens) multiply the same
-// vocabulary tile into two TMEM accumulators, so the 125 vocabulary tiles of a 32000-word head
-// run as one wave of 125 CTAs (a CTA per token tile made 250 CTAs of one per SM: two waves).
+// vocabulary tile into two TMEM accumulators (256 columns apart), so the 143 vocabulary tiles of
+// a 32000-word head run as one wave of 143 CTAs on the 148 SMs (a CTA per token tile made two
+// waves; 256-row tiles left 23 SMs idle with 8/7 of the work on the others).
 // One thread's bulk copies complete one after another (~0.4 us each on B200), so every copy of
 // a ring slot has its own issuing thread: lane 0 of warp 2 + 3 s streams slot s's vocabulary
 // tiles (the first before the dependency wait), lanes 0 of warps 3 + 3 s and 4 + 3 s its two
 // token tiles. Warp 1 issues the MMAs; warps 2..9 scan the accumulators, one token tile per
 // warp and 32 of its tokens (TMEM lane quarter warp % 4).
 constexpr int kLmStages = 3;
-constexpr int kLmBN = 256;  // vocabulary rows per tile
+constexpr int kLmBN = 224;  // vocabulary rows per tile (MMA N: a multiple of 16, <= 256)
 constexpr int kLmTT = 2;    // token tiles per CTA
+constexpr int kLmAcc = 256; // TMEM columns per token tile's accumulator (power-of-two allocation)
+static_assert(kLmBN <= kLmAcc && kLmBN % 32 == 0, "lm_head tile: accumulator columns, 32-column scan");
 constexpr int kLmCopies = 1 + kLmTT;  // bulk copies per ring slot
 struct LmCfg {
   static constexpr int kABytes = 128 * 64 * 2;    // one token tile
@@ -901,7 +904,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kLmTT * kLmBN);
+    tmem_alloc(tmem_slot, kLmTT * kLmAcc);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
@@ -957,7 +960,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
           const uint64_t ad = umma_desc_sw128(sA(s, tt));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + (uint32_t)(tt * kLmBN), ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+            umma_bf16(tmem + (uint32_t)(tt * kLmAcc), ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
         }
         umma_commit(&empty[s]);
       }
@@ -980,7 +983,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
       for (int c0 = 0; c0 < kLmBN; c0 += 32) {
         if (v0 + c0 >= p.V) break;  // warp-uniform
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tt * kLmBN + c0), v);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tt * kLmAcc + c0), v);
         tmem_ld_wait();
         uint32_t h[16];
 #pragma unroll
@@ -1018,7 +1021,7 @@ __global__ void __launch_bounds__(LmCfg::kThreads, 1) lm_head_argmax_kernel(cons
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kLmTT * kLmBN);
+    tmem_dealloc(tmem, kLmTT * kLmAcc);
   }
 }
 
